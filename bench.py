@@ -1,0 +1,418 @@
+"""Benchmark of the B200 attention path for tinylama (one JSON line on rank 0).
+
+Default workload (the batched multi-sequence decode): 256 independent sequences per GPU with
+context lengths drawn uniformly from [256, 4096] (seeded), Llama-2-7B-style attention (32 q
+heads, 32 kv heads, head_dim 128), one query token each, f32 KV cache.  A step is one decode
+step for every sequence: RoPE q/k at position L, append k/v at L, attention over L+1
+positions (src/forward.nim:314-317, batched).  The KV read per step (about 18 GB) is far
+larger than L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode_batched|decode_batched_bf16|decode_tiny|prefill|splitkv]
+
+N > 1 runs under torchrun, one process per GPU; sequences are sharded by batch (each rank its
+own 256 sequences, weak scaling) and timed as the max over ranks.  The `splitkv` workload
+splits one 131072-token context along the sequence axis across ranks and merges the (m, l, o)
+partials with NCCL.  `--impl reference` times the CPU oracle (a C restatement of the reference's
+attention; the reference itself is Nim and cannot be built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode attn tok/s"
+FALLBACK_HBM = 6650.0
+FALLBACK_TFLOPS = 1590.0
+
+
+# ---------------------------------------------------------------------------------- helpers
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "src": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM, "bf16_tflops": FALLBACK_TFLOPS,
+            "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def traffic_from_profiles(kernel_key: str):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    d = json.load(open(p)).get(kernel_key)
+    return None if d is None else d.get("dram_bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, backend="nccl"):
+        import torch
+        import datetime
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import torch.distributed as dist
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            import torch
+            self.pg.barrier(device_ids=[self.local])
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def seq_lens(seed: int, n: int, lo: int = 256, hi: int = 4096) -> np.ndarray:
+    return np.random.default_rng(seed).integers(lo, hi + 1, size=n).astype(np.int32)
+
+
+# ------------------------------------------------------------------- decode (batched) arm
+class DecodeBatched:
+    """256 sequences, 32/32 heads, head_dim 128, L ~ U[256, 4096], f32 (or bf16) KV."""
+
+    def __init__(self, kvd: int, rank: int, B=256, Hq=32, Hkv=32, D=128, base=10000.0):
+        import torch
+        from tinylama_b200 import _lib
+        self.torch, self._lib = torch, _lib
+        self.kvd, self.B, self.Hq, self.Hkv, self.D, self.base = kvd, B, Hq, Hkv, D, base
+        self.lens = seq_lens(1000 + rank, B)
+        self.maxLen = int(self.lens.max()) + 1
+        h = C.c_void_p()
+        _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, base, self.maxLen, B, kvd,
+                                           torch.cuda.current_device()))
+        self.h = h
+        # a real (non-null) stream: every torch op, library call and event below uses it
+        self.stream = torch.cuda.Stream()
+        torch.cuda.set_stream(self.stream)
+        g = torch.Generator(device="cuda").manual_seed(77 + rank)
+        for b in range(B):  # seeded N(0,1) K/V for positions [0, L_b)
+            L = int(self.lens[b])
+            k = torch.randn(L, Hkv * D, device="cuda", generator=g)
+            v = torch.randn(L, Hkv * D, device="cuda", generator=g)
+            _lib.check(_lib.lib.tl_kv_store(h, 0, b, 0, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
+                                            L, C.c_void_p(self.stream.cuda_stream)))
+        self.q = torch.randn(B, Hq * D, device="cuda", generator=g)
+        self.k = torch.randn(B, Hkv * D, device="cuda", generator=g)
+        self.v = torch.randn(B, Hkv * D, device="cuda", generator=g)
+        self.out = torch.empty(B, Hq * D, device="cuda")
+        self.pos_host = np.ascontiguousarray(self.lens)  # new token at position L
+        self.pos = torch.from_numpy(self.pos_host).cuda()
+        torch.cuda.synchronize()
+        _lib.check(_lib.lib.tl_check_device(h, None))
+
+    def ptr(self, t):
+        return C.c_void_p(t.data_ptr())
+
+    def step(self):
+        _l = self._lib
+        _l.check(_l.lib.tl_decode_step(self.h, 0, 0, self.B, self.ptr(self.pos),
+                                       self.pos_host.ctypes.data_as(C.c_void_p), self.ptr(self.q),
+                                       self.ptr(self.k), self.ptr(self.v), self.ptr(self.out),
+                                       C.c_void_p(self.stream.cuda_stream)))
+
+    def attention_only(self):
+        _l = self._lib
+        _l.check(_l.lib.tl_decode_attention(self.h, 0, 0, self.B, self.ptr(self.pos),
+                                            self.pos_host.ctypes.data_as(C.c_void_p), self.ptr(self.q),
+                                            self.ptr(self.out), C.c_void_p(self.stream.cuda_stream)))
+
+    launches_per_step = 2  # rope_append + decode
+
+    def kv_bytes(self) -> int:
+        es = 4 if self.kvd == 0 else 2
+        return int(np.sum(self.lens.astype(np.int64) + 1)) * self.Hkv * self.D * 2 * es
+
+    def algorithmic_bytes_attention(self) -> int:
+        # K and V rows read once + q read + ctx written (f32)
+        return self.kv_bytes() + 2 * self.B * self.Hq * self.D * 4
+
+    def flops(self) -> int:
+        return int(np.sum(self.lens.astype(np.int64) + 1)) * self.Hq * self.D * 4
+
+    def e2e(self, steps: int, warmup: int, dist: "Dist"):
+        """tl_decode_batch_host with pinned host buffers: H2D of q, k, v, positions and D2H of
+        the context inside every step."""
+        torch, _l = self.torch, self._lib
+        hq = torch.randn(self.B, self.Hq * self.D).pin_memory()
+        hk = torch.randn(self.B, self.Hkv * self.D).pin_memory()
+        hv = torch.randn(self.B, self.Hkv * self.D).pin_memory()
+        hout = torch.empty(self.B, self.Hq * self.D).pin_memory()
+        hpos = torch.from_numpy(self.pos_host.copy()).pin_memory()
+        p = lambda t: C.c_void_p(t.data_ptr())
+
+        def call():
+            _l.check(_l.lib.tl_decode_batch_host(self.h, 0, 0, self.B, p(hpos), p(hq), p(hk), p(hv), p(hout)))
+
+        for _ in range(warmup):
+            call()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            call()
+        dt = (time.perf_counter() - t0) / steps
+        dt = dist.max(dt)
+        h2d = hq.numel() * 4 + hk.numel() * 4 + hv.numel() * 4 + hpos.numel() * 4
+        d2h = hout.numel() * 4 + 4
+        return dt, h2d, d2h
+
+    def close(self):
+        self._lib.lib.tl_attn_destroy(self.h)
+
+
+def time_steps(fn, steps, warmup, stream, dist) -> float:
+    """Device time per call (ms) with CUDA events on the launching stream, max over ranks."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    return dist.max(ms)
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def cpu_decode_sample(lens, Hq, Hkv, D, base, budget_s: float, threads: int, seed: int = 5):
+    """Time the oracle's decode step (RoPE + store + attentionCached on the reference's f32
+    dim-major cache [nHeadKv*headDim, maxLen]) on a bounded sample of the sequences, `threads`
+    host threads in parallel (ctypes releases the GIL).  Inputs are generated before the timed
+    region.  Returns (sequences/s, sample description)."""
+    from oracle import oracle as ora
+    maxLen = int(np.max(lens)) + 1
+    rng = np.random.default_rng(seed)
+    bufs = []
+    for _ in range(threads):
+        kc = rng.standard_normal((Hkv * D, maxLen), dtype=np.float32)
+        vc = rng.standard_normal((Hkv * D, maxLen), dtype=np.float32)
+        bufs.append((kc, vc))
+    q = rng.standard_normal((Hq * D, 1), dtype=np.float32)
+    k = rng.standard_normal((Hkv * D, 1), dtype=np.float32)
+    v = rng.standard_normal((Hkv * D, 1), dtype=np.float32)
+    ora.lib()
+    # calibrate on one sequence, then size the sample to the budget
+    t0 = time.perf_counter()
+    ora.decode_step(q, k, v, bufs[0][0], bufs[0][1], int(lens[0]), Hq, Hkv, D, D, base)
+    t1 = time.perf_counter() - t0
+    n = int(max(threads, min(len(lens), budget_s / max(t1, 1e-6) * threads)))
+    n = (n // threads) * threads if n >= threads else n
+    order = [i % len(lens) for i in range(1, n + 1)]
+
+    def worker(t):
+        kc, vc = bufs[t]
+        for i in range(t, len(order), threads):
+            ora.decode_step(q, k, v, kc, vc, int(lens[order[i]]), Hq, Hkv, D, D, base)
+
+    ths = [threading.Thread(target=worker, args=(t,)) for t in range(threads)]
+    t0 = time.perf_counter()
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    wall = time.perf_counter() - t0
+    return len(order) / wall, (f"{len(order)} of {len(lens)} sequences per measurement "
+                               f"(oracle decode step, f32, reference layout, {threads} thread(s))")
+
+
+# ------------------------------------------------------------------------------ workloads
+def run_decode_batched(args, dist, kvd: int):
+    import torch
+    pk = peaks()
+    w = DecodeBatched(kvd, dist.rank)
+    sampler = ClockSampler(dist.local)
+    sampler.start()
+    ms = time_steps(w.step, args.steps, args.warmup, w.stream, dist)
+    clocks = sampler.stop()
+    ms_attn = time_steps(w.attention_only, args.steps, args.warmup, w.stream, dist)
+    n = dist.world
+    value = n * w.B / (ms / 1e3)
+    achieved = w.algorithmic_bytes_attention() / (ms_attn / 1e3) / 1e9
+    e2e_dt, h2d, d2h = w.e2e(max(3, args.steps // 4), 2, dist)
+    e2e_value = n * w.B / e2e_dt
+    traffic = traffic_from_profiles("decode_kernel_f32" if kvd == 0 else "decode_kernel_bf16")
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32" if kvd == 0 else "bf16-kv/f32-math", "data": "synthetic",
+        "config": {"workload": "batched multi-sequence decode (Llama-2-7B-style attention)",
+                   "seqs_per_gpu": w.B, "global_batch": w.B * n, "ctx_len": "U[256,4096] seeded",
+                   "mean_ctx": float(np.mean(w.lens)), "n_head": w.Hq, "n_head_kv": w.Hkv,
+                   "head_dim": w.D, "kv_dtype": "f32" if kvd == 0 else "bf16",
+                   "parallelism": f"batch-sharded x{n} (no collective)",
+                   "l2": f"no flush: {w.kv_bytes() / 1e9:.1f} GB of KV read per step >> 126 MB L2"},
+        "hbm_gbs_step": round(w.kv_bytes() / (ms / 1e3) / 1e9, 1),
+        "clocks": clocks,
+        "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "tl_decode_batch_host (pinned host buffers)"},
+        "gpu_launches": w.launches_per_step * args.steps,
+        "roofline": {"kernel": "decode_kernel", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "peak_src": pk["src"], "traffic": traffic,
+                     "algorithmic_bytes_per_launch": w.algorithmic_bytes_attention(),
+                     "launch_ms": round(ms_attn, 4)},
+    }
+    if n == 1 and dist.rank == 0 and not args.no_cpu_baseline:
+        rate, sample = cpu_decode_sample(w.lens, w.Hq, w.Hkv, w.D, w.base, args.cpu_budget, 1)
+        res["cpu_baseline"] = {"value": round(rate, 3), "unit": "tok/s", "cores": 1, "kind": "port",
+                               "sample": sample + "; Malebolgia on/off identical (attention has no "
+                                                  "Malebolgia path, src/forward.nim:51-74)"}
+    w.close()
+    return res
+
+
+def run_reference(args, dist):
+    """The reference arm: the oracle (C restatement of the reference's CPU attention) on all
+    host threads, rank 0 only, on a bounded sample of the same workload."""
+    if dist.rank != 0:
+        return None
+    B, Hq, Hkv, D, base = 256, 32, 32, 128, 10000.0
+    threads = os.cpu_count() or 1
+    lens = seq_lens(1000, B)
+    # size each step so that the whole run stays within a couple of minutes
+    per_step_budget = max(0.3, 90.0 / max(1, args.steps + args.warmup))
+    rates = []
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        r, sample = cpu_decode_sample(lens, Hq, Hkv, D, base, per_step_budget, threads, seed=i)
+        if i >= args.warmup:
+            rates.append(r)
+    value = statistics.median(rates)
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * B / value, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "batched multi-sequence decode (Llama-2-7B-style attention)",
+                   "seqs_per_gpu": B, "ctx_len": "U[256,4096] seeded", "n_head": Hq, "n_head_kv": Hkv,
+                   "head_dim": D, "kv_dtype": "f32"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"per step: {sample}, {threads} threads; the reference (Nim) "
+                                   "cannot be built here, this is its C restatement"},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="decode_batched",
+                    choices=["decode_batched", "decode_batched_bf16"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    dist = Dist()
+    if args.impl == "reference":
+        res = run_reference(args, dist)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    dist.init()
+    try:
+        if args.workload == "decode_batched":
+            res = run_decode_batched(args, dist, 0)
+        else:
+            res = run_decode_batched(args, dist, 1)
+        if dist.rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

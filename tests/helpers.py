@@ -1,0 +1,35 @@
+"""Shared test helpers: seeded inputs and the parity error metric."""
+from __future__ import annotations
+
+import numpy as np
+
+
+def randn(rng: np.random.Generator, *shape) -> np.ndarray:
+    return rng.standard_normal(shape).astype(np.float32)
+
+
+def max_rel_err(x: np.ndarray, r: np.ndarray) -> float:
+    """max_i |x_i - r_i| / max(|r_i|, 1e-3 * max_j |r_j|): elementwise relative error with a
+    floor, so that entries near zero do not dominate."""
+    x = np.asarray(x, np.float64)
+    r = np.asarray(r, np.float64)
+    floor = 1e-3 * max(float(np.max(np.abs(r))), 1e-30)
+    return float(np.max(np.abs(x - r) / np.maximum(np.abs(r), floor)))
+
+
+def normwise_err(x: np.ndarray, r: np.ndarray) -> float:
+    x = np.asarray(x, np.float64)
+    r = np.asarray(r, np.float64)
+    return float(np.max(np.abs(x - r)) / max(float(np.max(np.abs(r))), 1e-30))
+
+
+# Tolerances stated by the target: fp32-KV path and bf16-KV path.
+TOL_F32 = 1e-3
+TOL_BF16 = 2e-2
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bfloat16 -> float32 (the cache's storage rounding)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)

@@ -1,0 +1,60 @@
+"""The C-ABI library without a GPU: it loads, and it exports every function include/tl_attn.h
+declares (no compute calls)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "tl_attn.h")
+LIB = os.path.join(ROOT, "tinylama_b200", "libtlattn.so")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tl_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def built_lib():
+    if not os.path.exists(LIB):
+        from tinylama_b200 import build
+        build.build()
+    return ctypes.CDLL(LIB)
+
+
+def test_header_declares_the_reference_procs():
+    fns = declared_functions()
+    for name in ("tl_attn_create", "tl_rope_single_host", "tl_rope_at_pos_host", "tl_kv_store_host",
+                 "tl_attention_full_host", "tl_attention_cached_host", "tl_kv_clone"):
+        assert name in fns
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    missing = [f for f in declared_functions() if not hasattr(built_lib, f)]
+    assert not missing, missing
+
+
+def test_binding_table_matches_header(built_lib):
+    from tinylama_b200 import _lib
+    assert sorted(_lib.SIGNATURES) == declared_functions()
+
+
+def test_version_and_error_string_need_no_gpu(built_lib):
+    built_lib.tl_version.restype = ctypes.c_int
+    assert built_lib.tl_version() == 1
+    built_lib.tl_last_error.restype = ctypes.c_char_p
+    assert built_lib.tl_last_error() == b""
+
+
+def test_create_fails_cleanly_without_gpu_or_with_bad_shape(built_lib):
+    from tinylama_b200 import _lib
+    h = ctypes.c_void_p()
+    # nHead not divisible by nHeadKv: rejected before any device call, with the reference's text
+    rc = _lib.lib.tl_attn_create(ctypes.byref(h), 1, 6, 4, 64, 64, 10000.0, 16, 1, 0, 0)
+    assert rc == _lib.TL_ERR_INVALID
+    assert b"GQA requires head_count divisible by head_count_kv" in _lib.lib.tl_last_error()
+    rc = _lib.lib.tl_attn_create(ctypes.byref(h), 1, 32, 4, 96, 96, 10000.0, 16, 1, 0, 0)
+    assert rc == _lib.TL_ERR_UNSUPPORTED

@@ -1,0 +1,195 @@
+"""Device-tier (batched, token-major) entry points against the oracle, on a B200: the
+configurations of the batched decode (independent sequences of ragged length, 32 q = 32 kv
+heads, head_dim 128), long-context split-KV (32 q / 8 kv heads, theta 5e5) and the batched
+prefill (32 q / 8 kv heads, head_dim 64), at sizes the oracle finishes in seconds."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import oracle as ora
+from tests.helpers import TOL_BF16, TOL_F32, bf16_round, max_rel_err, randn
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def env(cuda_lib):
+    import torch
+    from tinylama_b200 import _lib
+    return torch, _lib
+
+
+def create(_lib, nLayer, Hq, Hkv, D, maxLen, maxBatch, kvd, base=10000.0):
+    h = C.c_void_p()
+    _lib.check(_lib.lib.tl_attn_create(C.byref(h), nLayer, Hq, Hkv, D, D, base, maxLen, maxBatch, kvd, 0))
+    return h
+
+
+def ptr(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def fill_cache(torch, _lib, h, layer, lens, Hkv, D, rng, base, kvd):
+    """Write seeded K/V for every slot via tl_kv_store_host; return oracle-layout caches."""
+    caches = []
+    for b, L in enumerate(lens):
+        k = randn(rng, Hkv * D, L)
+        v = randn(rng, Hkv * D, L)
+        kr = ora.rope_single(k, Hkv, D, D, base)  # cached keys carry their RoPE
+        _lib.check(_lib.lib.tl_kv_store_host(h, layer, b, 0, kr.ctypes.data_as(C.c_void_p),
+                                             v.ctypes.data_as(C.c_void_p), L))
+        if kvd == 1:
+            kr, v = bf16_round(kr), bf16_round(v)
+        caches.append((kr, v))
+    return caches
+
+
+@pytest.mark.parametrize("kvd", [0, 1])
+@pytest.mark.parametrize("Hq,Hkv,D,lens", [
+    (32, 32, 128, [256, 1000, 4095, 300, 2049, 31, 1]),  # ragged batch, head_dim 128
+    (32, 4, 64, [128, 512, 2048]),                       # TinyLlama GQA 8:1
+    (32, 8, 128, [5000, 77]),                            # GQA 4:1, multi-chunk
+])
+def test_decode_step_batched(env, kvd, Hq, Hkv, D, lens):
+    torch, _lib = env
+    rng = np.random.default_rng(sum(lens) + kvd)
+    base = 10000.0
+    B = len(lens)
+    maxLen = max(lens) + 2
+    h = create(_lib, 2, Hq, Hkv, D, maxLen, B, kvd, base)
+    try:
+        caches = fill_cache(torch, _lib, h, 1, lens, Hkv, D, rng, base, kvd)
+        q = randn(rng, B, Hq * D)
+        k = randn(rng, B, Hkv * D)
+        v = randn(rng, B, Hkv * D)
+        pos = np.array(lens, np.int32)  # new token at position L, attends L+1 positions
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        dpos = torch.from_numpy(pos).cuda()
+        out = torch.empty(B, Hq * D, device="cuda")
+        _lib.check(_lib.lib.tl_decode_step(h, 1, 0, B, ptr(dpos), pos.ctypes.data_as(C.c_void_p),
+                                           ptr(dq), ptr(dk), ptr(dv), ptr(out), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+        got = out.cpu().numpy()
+        for b, L in enumerate(lens):
+            qr = ora.rope_at_pos(q[b].reshape(-1, 1), Hq, D, D, base, L)
+            kr = ora.rope_at_pos(k[b].reshape(-1, 1), Hkv, D, D, base, L)
+            kc = np.zeros((Hkv * D, L + 1), np.float32)
+            vc = np.zeros((Hkv * D, L + 1), np.float32)
+            kc[:, :L], vc[:, :L] = caches[b]
+            kc[:, L:] = kr if kvd == 0 else bf16_round(kr)
+            vc[:, L:] = v[b].reshape(-1, 1) if kvd == 0 else bf16_round(v[b].reshape(-1, 1))
+            ref = ora.attention_cached(qr, kc, vc, L + 1, Hq, Hkv, D)
+            assert max_rel_err(got[b].reshape(-1, 1), ref) <= TOL_F32, (b, L, max_rel_err(got[b].reshape(-1, 1), ref))
+        # repeated calls give identical results (counters are reset by the merging CTA)
+        out2 = torch.empty_like(out)
+        dq2, dk2 = (torch.from_numpy(a).cuda() for a in (q, k))
+        _lib.check(_lib.lib.tl_decode_step(h, 1, 0, B, ptr(dpos), None, ptr(dq2), ptr(dk2), ptr(dv),
+                                           ptr(out2), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+        assert torch.allclose(out2, out, rtol=1e-5, atol=1e-6)
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
+def test_decode_batch_host_matches_device_tier(env):
+    torch, _lib = env
+    rng = np.random.default_rng(21)
+    lens = [700, 33, 1500, 256]
+    B, Hq, Hkv, D = 4, 32, 32, 128
+    h = create(_lib, 1, Hq, Hkv, D, 2048, B, 0)
+    try:
+        fill_cache(torch, _lib, h, 0, lens, Hkv, D, rng, 10000.0, 0)
+        q, k, v = randn(rng, B, Hq * D), randn(rng, B, Hkv * D), randn(rng, B, Hkv * D)
+        pos = np.array(lens, np.int32)
+        out = np.empty((B, Hq * D), np.float32)
+        f = lambda a: a.ctypes.data_as(C.c_void_p)
+        _lib.check(_lib.lib.tl_decode_batch_host(h, 0, 0, B, f(pos), f(q), f(k), f(v), f(out)))
+        for b, L in enumerate(lens):
+            assert out[b].any()
+        # same inputs through the device tier
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        dpos = torch.from_numpy(pos).cuda()
+        o2 = torch.empty(B, Hq * D, device="cuda")
+        _lib.check(_lib.lib.tl_decode_step(h, 0, 0, B, ptr(dpos), f(pos), ptr(dq), ptr(dk), ptr(dv), ptr(o2), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+        assert np.allclose(o2.cpu().numpy(), out, rtol=1e-5, atol=1e-6)
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
+def test_device_error_word_reports_bad_position(env):
+    """A position past maxLen given only on the device is caught by the kernel's bounds check
+    (no write happens) and reported through tl_check_device."""
+    torch, _lib = env
+    h = create(_lib, 1, 32, 4, 64, 16, 1, 0)
+    try:
+        dpos = torch.tensor([16], dtype=torch.int32, device="cuda")
+        q = torch.zeros(1, 2048, device="cuda")
+        k = torch.zeros(1, 256, device="cuda")
+        out = torch.empty(1, 2048, device="cuda")
+        rc = _lib.lib.tl_decode_step(h, 0, 0, 1, ptr(dpos), None, ptr(q), ptr(k), ptr(k), ptr(out), None)
+        if rc == _lib.TL_OK:
+            rc = _lib.lib.tl_check_device(h, None)
+        assert rc == _lib.TL_ERR_DEVICE
+        assert b"position-out-of-range" in _lib.lib.tl_last_error()
+        # the handle stays usable
+        dpos.fill_(3)
+        _lib.check(_lib.lib.tl_decode_attention(h, 0, 0, 1, ptr(dpos), None, ptr(q), ptr(out), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
+@pytest.mark.parametrize("kvd,S", [(0, 64), (0, 200), (1, 128), (1, 300)])
+def test_prefill_step_batched(env, kvd, S):
+    torch, _lib = env
+    rng = np.random.default_rng(S + kvd)
+    B, Hq, Hkv, D = 2, 32, 8, 64
+    h = create(_lib, 1, Hq, Hkv, D, S, B, kvd)
+    try:
+        q, k, v = randn(rng, B, S, Hq * D), randn(rng, B, S, Hkv * D), randn(rng, B, S, Hkv * D)
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        out = torch.empty(B, S, Hq * D, device="cuda")
+        _lib.check(_lib.lib.tl_prefill_step(h, 0, 0, B, S, ptr(dq), ptr(dk), ptr(dv), ptr(out), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+        got = out.cpu().numpy()
+        tol = TOL_F32 if kvd == 0 else TOL_BF16
+        for b in range(B):
+            qc = np.ascontiguousarray(q[b].T)
+            kc = np.ascontiguousarray(k[b].T)
+            vc = np.ascontiguousarray(v[b].T)
+            qr = ora.rope_single(qc, Hq, D, D, 10000.0)
+            kr = ora.rope_single(kc, Hkv, D, D, 10000.0)
+            ref = ora.attention_full_ctx(qr, kr, vc, Hq, Hkv, D)
+            err = max_rel_err(np.ascontiguousarray(got[b].T), ref)
+            assert err <= tol, (b, err)
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
+def test_dist_single_rank_matches_local(env):
+    """tl_decode_attention_dist with one rank: the (m, l, o) partial path, the NCCL all-gather
+    and the merge kernel must reproduce the single-GPU result."""
+    torch, _lib = env
+    rng = np.random.default_rng(31)
+    lens = [3000, 129, 1]
+    B, Hq, Hkv, D = 3, 32, 8, 128
+    h = create(_lib, 1, Hq, Hkv, D, 4096, B, 1, 500000.0)
+    try:
+        fill_cache(torch, _lib, h, 0, lens, Hkv, D, rng, 500000.0, 1)
+        uid = C.create_string_buffer(128)
+        _lib.check(_lib.lib.tl_dist_unique_id(uid))
+        _lib.check(_lib.lib.tl_dist_init(h, uid, 1, 0))
+        q = torch.from_numpy(randn(rng, B, Hq * D)).cuda()
+        pos = np.array([L - 1 for L in lens], np.int32)
+        dpos = torch.from_numpy(pos).cuda()
+        o1 = torch.empty(B, Hq * D, device="cuda")
+        o2 = torch.empty(B, Hq * D, device="cuda")
+        f = pos.ctypes.data_as(C.c_void_p)
+        _lib.check(_lib.lib.tl_decode_attention(h, 0, 0, B, ptr(dpos), f, ptr(q), ptr(o1), None))
+        _lib.check(_lib.lib.tl_decode_attention_dist(h, 0, 0, B, ptr(dpos), f, ptr(q), ptr(o2), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+        assert torch.allclose(o1, o2, rtol=1e-4, atol=1e-5)
+    finally:
+        _lib.lib.tl_attn_destroy(h)

@@ -1,0 +1,546 @@
+// decode_attn.cu -- split-KV ("flash-decoding") decode attention over the head-major cache.
+//
+// Replaces attentionCached (src/forward.nim:179-211): for every q-head h of a sequence,
+//   s_j = q_h . k_{kvh,j} / sqrt(d),  p = softmax(s over j < curLen),  ctx_h = sum_j p_j v_{kvh,j}
+// with kvh = h / (nHead / nHeadKv).  The reference reads the dim-major cache with stride
+// maxLen and re-reads each kv-head once per q-head; here one CTA work unit (sequence, kv-head,
+// chunk of positions) reads each K/V row from HBM once and serves all G = nHead/nHeadKv
+// q-heads of the group.
+//
+// Structure (persistent kernel, grid = CTAs resident on the device):
+//   * warp 4 (producer): streams contiguous K and V tiles of T positions (head-major layout
+//     makes a tile one contiguous block) with cp.async.bulk into an NS-stage shared-memory
+//     ring guarded by full/empty mbarriers.  No tensor map, no multicast.
+//   * warps 0..3 (consumers): each owns PPW = T/4 positions of every tile, computes the G*PPW
+//     dot products with lanes over head_dim, reduces them with a multi-value butterfly
+//     (log2 shuffles per value), and keeps its own online-softmax state (m, l, o) in the
+//     log2 domain.  At the end of a unit the four warp states are merged through shared
+//     memory.
+//   * a unit that covers a whole sequence writes ctx directly; otherwise it writes its
+//     (o, m, l) partial to scratch and the last CTA to finish a (sequence, kv-head) merges
+//     all chunks (threadfence + arrival counter; nobody waits on anybody).
+#include <float.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace tl {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxChunksPerSeq = 256;
+
+template <typename KV, int D, int G>
+struct DecCfg {
+    static constexpr int VPL = D / 32;          // head_dim values per lane
+    static constexpr int T = 32;                // positions per tile
+    static constexpr int NW = 4;                // consumer warps
+    static constexpr int PPW = T / NW;          // positions per warp per tile
+    static constexpr int NV = G * PPW;          // dot products per warp per tile
+    static constexpr int THREADS = 32 * (NW + 1);
+    static constexpr int TILE_BYTES = T * D * (int)sizeof(KV);
+    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+    static constexpr int NS_RAW = 98304 / STAGE_BYTES;
+    static constexpr int NS = NS_RAW < 2 ? 2 : (NS_RAW > 8 ? 8 : NS_RAW);
+    // shared memory carve-up (bytes, all 16-aligned)
+    static constexpr int OFF_STAGES = 0;
+    static constexpr int OFF_BARS = OFF_STAGES + NS * STAGE_BYTES;
+    static constexpr int OFF_SC = OFF_BARS + 2 * NS * 8 + 16;           // [NW][NV] scores
+    static constexpr int OFF_WM = OFF_SC + NW * NV * 4;                 // [NW][G] m
+    static constexpr int OFF_WL = OFF_WM + NW * G * 4;                  // [NW][G] l
+    static constexpr int OFF_WO = OFF_WL + NW * G * 4;                  // [NW][G][D] o
+    static constexpr int OFF_CW = OFF_WO + NW * G * D * 4;              // [256][G] chunk weights
+    static constexpr int OFF_PREFIX = OFF_CW + kMaxChunksPerSeq * G * 4;
+    static size_t smem_bytes(int nseq) { return (size_t)OFF_PREFIX + 4 * (size_t)(nseq + 1) + 16; }
+};
+
+__device__ __forceinline__ float safe_exp2_diff(float m, float M) {
+    return (m == -INFINITY) ? 0.f : exp2f(m - M);
+}
+
+// Multi-value butterfly: N partial sums per lane -> after the call, lane holds the full
+// (over 32 lanes) sum of R = max(1, N/32) of the N values in v[0..R).  The original index of
+// v[r] is butterfly_index<N>(lane) + r.
+template <int N>
+__device__ __forceinline__ void butterfly(float (&v)[N], int lane) {
+    int h = N / 2;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        if (h >= 1) {
+            const bool upper = (lane & m) != 0;
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) {
+                if (i < h) {
+                    const float send = upper ? v[i] : v[i + h];
+                    const float keep = upper ? v[i + h] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+                }
+            }
+            h >>= 1;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+        }
+    }
+}
+template <int N>
+__device__ __forceinline__ int butterfly_index(int lane) {
+    int idx = 0, h = N / 2;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        if (h >= 1) {
+            if (lane & m) idx += h;
+            h >>= 1;
+        }
+    }
+    return idx;
+}
+
+__device__ __forceinline__ size_t decode_partial_floats_dev(int total_units, int group, int d) {
+    return (size_t)total_units * group * (d + 2);
+}
+
+struct Unit {
+    int b, g, c, nch, n, p0, p1;
+};
+
+__device__ __forceinline__ int local_len(const DecodeArgs &a, int b, unsigned *err) {
+    const int pos = a.pos[b];
+    const int slice = a.kv.maxLen;
+    if (pos < 0 || pos - a.pos_offset >= slice) {
+        // single-GPU: the appended token must sit inside the cache
+        if (a.lse_out == nullptr || pos < 0) atomicOr(err, TL_DEVERR_POS_RANGE);
+    }
+    int n = pos + 1 - a.pos_offset;
+    n = n < 0 ? 0 : (n > slice ? slice : n);
+    return n;
+}
+
+__device__ __forceinline__ int nchunks(int n, int C) { return n <= 0 ? 1 : (n + C - 1) / C; }
+
+__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, const int *prefix, const int *lens,
+                                            int u) {
+    Unit r;
+    r.g = u % a.nHeadKv;
+    const int t = u / a.nHeadKv;
+    // upper_bound over prefix[0..nseq] for t
+    int lo = 0, hi = a.nseq;  // prefix[lo] <= t < prefix[hi]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (prefix[mid] <= t) lo = mid; else hi = mid;
+    }
+    r.b = lo;
+    r.c = t - prefix[lo];
+    r.nch = prefix[lo + 1] - prefix[lo];
+    r.n = lens[lo];
+    r.p0 = r.c * a.chunk;
+    r.p1 = min(r.p0 + a.chunk, r.n);
+    if (r.p1 < r.p0) r.p1 = r.p0;
+    return r;
+}
+
+template <typename KV, int D, int G>
+__global__ void __launch_bounds__(DecCfg<KV, D, G>::THREADS)
+decode_kernel(const DecodeArgs a) {
+    using C = DecCfg<KV, D, G>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::OFF_BARS);
+    uint64_t *empty = full + C::NS;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + C::NS);
+    int *is_last_flag = const_cast<int *>(reinterpret_cast<volatile int *>(abort_flag) + 1);
+    int *max_nch = is_last_flag + 1;
+    float *sc = reinterpret_cast<float *>(smem + C::OFF_SC);
+    float *wm = reinterpret_cast<float *>(smem + C::OFF_WM);
+    float *wl = reinterpret_cast<float *>(smem + C::OFF_WL);
+    float *wo = reinterpret_cast<float *>(smem + C::OFF_WO);
+    float *cw = reinterpret_cast<float *>(smem + C::OFF_CW);
+    int *prefix = reinterpret_cast<int *>(smem + C::OFF_PREFIX);
+    // lens are kept in the high part of the prefix region: prefix[nseq+1], lens after it
+    int *lens = prefix + (a.nseq + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    unsigned *err = a.err;
+
+    // ---- schedule: per-sequence chunk counts and their exclusive prefix (warp 0) ----------
+    if (tid == 0) {
+        for (int s = 0; s < C::NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], C::NW);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        const int per = (a.nseq + 31) / 32;
+        const int s0 = lane * per, s1 = min(s0 + per, a.nseq);
+        int sum = 0, mx = 0;
+        for (int s = s0; s < s1; ++s) {
+            const int n = local_len(a, s, err);
+            lens[s] = n;
+            sum += nchunks(n, a.chunk);
+            mx = max(mx, nchunks(n, a.chunk));
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) max_nch[0] = mx;
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int run = incl - sum;
+        for (int s = s0; s < s1; ++s) {
+            prefix[s] = run;
+            run += nchunks(lens[s], a.chunk);
+        }
+        if (lane == 31) prefix[a.nseq] = incl;
+    }
+    __syncthreads();
+    const int total_units = prefix[a.nseq] * a.nHeadKv;
+    // The host sizes the scratch and the chunk length; refuse (uniformly) if they do not fit.
+    if (max_nch[0] > kMaxChunksPerSeq ||
+        (max_nch[0] > 1 && decode_partial_floats_dev(total_units, G, D) > a.partial_cap)) {
+        if (tid == 0) atomicOr(err, TL_DEVERR_BAD_ARG);
+        return;
+    }
+    const float qscale = kLog2e / sqrtf((float)D);
+
+    if (warp == C::NW) {
+        // ================= producer ==================
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int stage = 0;
+            uint32_t phase = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+                const Unit un = decode_unit(a, prefix, lens, u);
+                const int64_t row0 = a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
+                const KV *kb = reinterpret_cast<const KV *>(a.kv.k) + row0 * D;
+                const KV *vb = reinterpret_cast<const KV *>(a.kv.v) + row0 * D;
+                for (int p = un.p0; p < un.p1; p += C::T) {
+                    const int np = min(C::T, un.p1 - p);
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, abort_flag)) { ok = false; break; }
+                    const uint32_t bytes = (uint32_t)(np * D * sizeof(KV));
+                    uint8_t *st = smem + C::OFF_STAGES + stage * C::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], 2 * bytes);
+                    bulk_g2s_evict_first(st, kb + (int64_t)p * D, bytes, &full[stage], pol);
+                    bulk_g2s_evict_first(st + C::TILE_BYTES, vb + (int64_t)p * D, bytes, &full[stage], pol);
+                    ++issued;
+                    if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) {
+                // drain: wait (bounded) for the copies this thread issued into the ring
+                const int outstanding = issued < (long)C::NS ? (int)issued : C::NS;
+                int s = stage;
+                uint32_t ph = phase;
+                for (int i = 0; i < outstanding; ++i) {
+                    if (--s < 0) { s = C::NS - 1; ph ^= 1u; }
+                    mbar_wait(&full[s], ph, err, nullptr);
+                }
+            }
+        }
+        return;
+    }
+
+    // ================= consumers ==================
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+        const Unit un = decode_unit(a, prefix, lens, u);
+        // q for the G heads of this group, pre-scaled so that scores are in log2 units
+        float qf[G][C::VPL];
+        const float *qrow = a.q + ((int64_t)un.b * a.nHead + (int64_t)un.g * G) * D + lane * C::VPL;
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+#pragma unroll
+            for (int v = 0; v < C::VPL; ++v) qf[h][v] = qrow[(int64_t)h * D + v] * qscale;
+        }
+        float m[G], l[G], o[G][C::VPL];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            m[h] = -INFINITY;
+            l[h] = 0.f;
+#pragma unroll
+            for (int v = 0; v < C::VPL; ++v) o[h][v] = 0.f;
+        }
+        bool ok = true;
+        for (int p = un.p0; p < un.p1; p += C::T) {
+            const int np = min(C::T, un.p1 - p);
+            if (!mbar_wait(&full[stage], phase, err, abort_flag)) { ok = false; break; }
+            const KV *ks = reinterpret_cast<const KV *>(smem + C::OFF_STAGES + stage * C::STAGE_BYTES);
+            const KV *vs = reinterpret_cast<const KV *>(smem + C::OFF_STAGES + stage * C::STAGE_BYTES + C::TILE_BYTES);
+            const int jb = warp * C::PPW;
+            // dot products: part[h*PPW + jj]
+            float part[C::NV];
+#pragma unroll
+            for (int jj = 0; jj < C::PPW; ++jj) {
+                float kv[C::VPL];
+                VecLoad<KV, C::VPL>::run(ks + (jb + jj) * D + lane * C::VPL, kv);
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int v = 0; v < C::VPL; ++v) acc = fmaf(qf[h][v], kv[v], acc);
+                    part[h * C::PPW + jj] = acc;
+                }
+            }
+            butterfly<C::NV>(part, lane);
+            {
+                const int base = butterfly_index<C::NV>(lane);
+                constexpr int R = C::NV >= 32 ? C::NV / 32 : 1;
+#pragma unroll
+                for (int r = 0; r < R; ++r) sc[warp * C::NV + base + r] = part[r];
+            }
+            __syncwarp();
+            float pr[G][C::PPW];
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                float s[C::PPW];
+#pragma unroll
+                for (int jj = 0; jj < C::PPW; jj += 4) {
+                    const float4 t4 = *reinterpret_cast<const float4 *>(&sc[warp * C::NV + h * C::PPW + jj]);
+                    s[jj] = t4.x; s[jj + 1] = t4.y; s[jj + 2] = t4.z; s[jj + 3] = t4.w;
+                }
+                float tmax = -INFINITY;
+#pragma unroll
+                for (int jj = 0; jj < C::PPW; ++jj) {
+                    if (jb + jj >= np) s[jj] = -INFINITY;
+                    tmax = fmaxf(tmax, s[jj]);
+                }
+                const float mnew = fmaxf(m[h], tmax);
+                const float alpha = safe_exp2_diff(m[h], mnew);
+                float psum = 0.f;
+#pragma unroll
+                for (int jj = 0; jj < C::PPW; ++jj) {
+                    pr[h][jj] = (s[jj] == -INFINITY) ? 0.f : exp2f(s[jj] - mnew);
+                    psum += pr[h][jj];
+                }
+                l[h] = l[h] * alpha + psum;
+                m[h] = mnew;
+#pragma unroll
+                for (int v = 0; v < C::VPL; ++v) o[h][v] *= alpha;
+            }
+#pragma unroll
+            for (int jj = 0; jj < C::PPW; ++jj) {
+                if (jb + jj < np) {
+                    float vv[C::VPL];
+                    VecLoad<KV, C::VPL>::run(vs + (jb + jj) * D + lane * C::VPL, vv);
+#pragma unroll
+                    for (int h = 0; h < G; ++h) {
+#pragma unroll
+                        for (int v = 0; v < C::VPL; ++v) o[h][v] = fmaf(pr[h][jj], vv[v], o[h][v]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+        }
+        // ---- merge the four warp states (reached even after an abort, so that every
+        // consumer warp arrives at the same named barriers) ----
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            if (lane == 0) { wm[warp * G + h] = m[h]; wl[warp * G + h] = l[h]; }
+#pragma unroll
+            for (int v = 0; v < C::VPL; ++v) wo[(warp * G + h) * D + lane * C::VPL + v] = o[h][v];
+        }
+        named_bar(1, C::NW * 32);
+        const bool single = (un.nch == 1) && (a.lse_out == nullptr);
+        const int unit_index = u;  // partial slot of this unit
+        for (int e = tid; e < G * D; e += C::NW * 32) {
+            const int h = e / D, dd = e - h * D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < C::NW; ++w) M = fmaxf(M, wm[w * G + h]);
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (int w = 0; w < C::NW; ++w) {
+                const float sw = safe_exp2_diff(wm[w * G + h], M);
+                L = fmaf(wl[w * G + h], sw, L);
+                O = fmaf(wo[(w * G + h) * D + dd], sw, O);
+            }
+            const int head = un.g * G + h;
+            if (single) {
+                a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
+            } else if (un.nch == 1) {
+                float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);
+                dst[dd] = O;
+                if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
+            } else {
+                float *dst = a.partial + ((int64_t)unit_index * G + h) * (D + 2);
+                dst[dd] = O;
+                if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
+            }
+        }
+        if (un.nch > 1) {
+            __threadfence();
+            named_bar(1, C::NW * 32);
+            if (tid == 0) {
+                const unsigned old = atomicAdd(&a.counter[un.b * a.nHeadKv + un.g], 1u);
+                *is_last_flag = (old == (unsigned)(un.nch - 1)) ? 1 : 0;
+            }
+            named_bar(1, C::NW * 32);
+            if (*is_last_flag) {
+                __threadfence();
+                // per-head max / sum over the chunks (warp h handles heads h, h+4, ...)
+                for (int h = warp; h < G; h += C::NW) {
+                    float M = -INFINITY;
+                    for (int c = lane; c < un.nch; c += 32) {
+                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
+                        M = fmaxf(M, __ldcg(&a.partial[((int64_t)uc * G + h) * (D + 2) + D]));
+                    }
+#pragma unroll
+                    for (int o2 = 16; o2 >= 1; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+                    float L = 0.f;
+                    for (int c = lane; c < un.nch; c += 32) {
+                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
+                        const float *pp = &a.partial[((int64_t)uc * G + h) * (D + 2) + D];
+                        const float w = safe_exp2_diff(__ldcg(pp), M);
+                        cw[c * G + h] = w;
+                        L = fmaf(__ldcg(pp + 1), w, L);
+                    }
+#pragma unroll
+                    for (int o2 = 16; o2 >= 1; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+                    if (lane == 0) { wm[h] = M; wl[h] = L; }
+                }
+                named_bar(1, C::NW * 32);
+                for (int e = tid; e < G * D; e += C::NW * 32) {
+                    const int h = e / D, dd = e - h * D;
+                    float O = 0.f;
+                    for (int c = 0; c < un.nch; ++c) {
+                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
+                        O = fmaf(cw[c * G + h], __ldcg(&a.partial[((int64_t)uc * G + h) * (D + 2) + dd]), O);
+                    }
+                    const int head = un.g * G + h;
+                    const float L = wl[h];
+                    if (a.lse_out == nullptr) {
+                        a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
+                    } else {
+                        float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);
+                        dst[dd] = O;
+                        if (dd == 0) { dst[D] = wm[h]; dst[D + 1] = L; }
+                    }
+                }
+                if (tid == 0) a.counter[un.b * a.nHeadKv + un.g] = 0u;
+            }
+        }
+        // shared scratch is reused by the next unit; leave together if any warp aborted
+        if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
+    }
+}
+
+// Merge G per-rank (o, m, l) partials into the final context.
+__global__ void lse_merge_kernel(const float *__restrict__ parts, int nparts, int rows, int D,
+                                 float *__restrict__ out) {
+    const int row = blockIdx.x;
+    if (row >= rows) return;
+    const int64_t stride_rank = (int64_t)rows * (D + 2);
+    float M = -INFINITY;
+    for (int r = 0; r < nparts; ++r) M = fmaxf(M, parts[r * stride_rank + (int64_t)row * (D + 2) + D]);
+    float L = 0.f;
+    for (int r = 0; r < nparts; ++r) {
+        const float *pp = parts + r * stride_rank + (int64_t)row * (D + 2);
+        L = fmaf(pp[D + 1], safe_exp2_diff(pp[D], M), L);
+    }
+    for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
+        float O = 0.f;
+        for (int r = 0; r < nparts; ++r) {
+            const float *pp = parts + r * stride_rank + (int64_t)row * (D + 2);
+            O = fmaf(pp[dd], safe_exp2_diff(pp[D], M), O);
+        }
+        out[(int64_t)row * D + dd] = (L > 0.f) ? O / L : 0.f;
+    }
+}
+
+template <typename KV, int D, int G>
+cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
+    using C = DecCfg<KV, D, G>;
+    const size_t smem = C::smem_bytes(a.nseq) + 4 * (size_t)a.nseq;
+    auto kern = decode_kernel<KV, D, G>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<num_ctas, C::THREADS, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <typename KV, int D>
+cudaError_t launch_g(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
+    switch (a.nHead / a.nHeadKv) {
+        case 1: return launch_t<KV, D, 1>(a, num_ctas, s);
+        case 2: return launch_t<KV, D, 2>(a, num_ctas, s);
+        case 4: return launch_t<KV, D, 4>(a, num_ctas, s);
+        case 8: return launch_t<KV, D, 8>(a, num_ctas, s);
+        default: return cudaErrorNotSupported;
+    }
+}
+
+template <typename KV, int D, int G>
+int occ_t() {
+    using C = DecCfg<KV, D, G>;
+    int n = 0;
+    const size_t smem = C::smem_bytes(256) + 4 * 256;
+    cudaFuncSetAttribute(decode_kernel<KV, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<KV, D, G>, C::THREADS, smem) != cudaSuccess) n = 1;
+    return n < 1 ? 1 : n;
+}
+
+}  // namespace
+
+cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
+    if (a.headDim == 64) {
+        return a.kv.dtype == TL_KV_F32 ? launch_g<float, 64>(a, num_ctas, s)
+                                       : launch_g<__nv_bfloat16, 64>(a, num_ctas, s);
+    }
+    if (a.headDim == 128) {
+        return a.kv.dtype == TL_KV_F32 ? launch_g<float, 128>(a, num_ctas, s)
+                                       : launch_g<__nv_bfloat16, 128>(a, num_ctas, s);
+    }
+    return cudaErrorNotSupported;
+}
+
+static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype);
+
+int decode_ctas_per_sm(int headDim, int group, int dtype) {
+    // occupancy of each kernel instance, queried once per process and device
+    static int cache[16][2][2][9];  // [device][headDim 64/128][dtype][group]
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 16 || group < 1 || group > 8) return decode_ctas_per_sm_uncached(headDim, group, dtype);
+    int &slot = cache[dev][headDim == 128][dtype == TL_KV_BF16][group];
+    if (slot == 0) slot = decode_ctas_per_sm_uncached(headDim, group, dtype);
+    return slot;
+}
+
+static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype) {
+#define TL_OCC(KV, D)                                  \
+    switch (group) {                                   \
+        case 1: return occ_t<KV, D, 1>();              \
+        case 2: return occ_t<KV, D, 2>();              \
+        case 4: return occ_t<KV, D, 4>();              \
+        case 8: return occ_t<KV, D, 8>();              \
+        default: return 1;                             \
+    }
+    if (headDim == 64) {
+        if (dtype == TL_KV_F32) { TL_OCC(float, 64) } else { TL_OCC(__nv_bfloat16, 64) }
+    } else if (headDim == 128) {
+        if (dtype == TL_KV_F32) { TL_OCC(float, 128) } else { TL_OCC(__nv_bfloat16, 128) }
+    }
+#undef TL_OCC
+    return 1;
+}
+
+size_t decode_partial_floats(int total_units, int group, int headDim) {
+    return (size_t)total_units * group * (headDim + 2);
+}
+
+cudaError_t launch_lse_merge(const float *parts, int nparts, int nseq, int nHead, int headDim,
+                             float *out, cudaStream_t s) {
+    const int rows = nseq * nHead;
+    lse_merge_kernel<<<rows, headDim, 0, s>>>(parts, nparts, rows, headDim, out);
+    return cudaGetLastError();
+}
+
+}  // namespace tl

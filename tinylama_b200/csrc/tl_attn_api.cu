@@ -1,0 +1,787 @@
+// tl_attn_api.cu -- the C ABI of libtlattn.so (declared in include/tl_attn.h).
+//
+// Host-side runtime around the kernels: handle and KV-cache ownership, argument validation
+// with the reference's error messages, the split-KV schedule, host<->device staging for the
+// host tier, and the device error word.  No CPU fallback exists anywhere in this library: if
+// a shape has no kernel the call fails with TL_ERR_UNSUPPORTED.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace tl;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define TL_CUDA(call)                                                                         \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess)                                                                \
+            return fail(e_ == cudaErrorMemoryAllocation ? TL_ERR_NOMEM : TL_ERR_CUDA,         \
+                        "%s failed: %s", #call, cudaGetErrorString(e_));                      \
+    } while (0)
+
+#define TL_TRY(expr)            \
+    do {                        \
+        int r_ = (expr);        \
+        if (r_ != TL_OK) return r_; \
+    } while (0)
+
+// Makes the handle's device current for the scope and restores the caller's device.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+size_t esize(int dtype) { return dtype == TL_KV_BF16 ? 2 : 4; }
+
+bool supported_group(int g) { return g == 1 || g == 2 || g == 4 || g == 8; }
+
+int check_shape(int nHead, int nHeadKv, int headDim) {
+    if (nHead <= 0 || nHeadKv <= 0)
+        return fail(TL_ERR_INVALID, "KV cache requires llama-style head_count");
+    if (nHead % nHeadKv != 0)
+        return fail(TL_ERR_INVALID, "GQA requires head_count divisible by head_count_kv");
+    if (headDim != 64 && headDim != 128)
+        return fail(TL_ERR_UNSUPPORTED, "headDim %d: kernels are built for 64 and 128", headDim);
+    if (!supported_group(nHead / nHeadKv))
+        return fail(TL_ERR_UNSUPPORTED, "GQA group %d: kernels are built for 1, 2, 4 and 8",
+                    nHead / nHeadKv);
+    return TL_OK;
+}
+
+int check_handle_shape(const tl_attn *h, int nHead, int nHeadKv, int headDim) {
+    if (nHead != h->nHead || nHeadKv != h->nHeadKv || headDim != h->headDim)
+        return fail(TL_ERR_INVALID,
+                    "shape (%d,%d,%d) does not match the cache's (nHead %d, nHeadKv %d, headDim %d)",
+                    nHead, nHeadKv, headDim, h->nHead, h->nHeadKv, h->headDim);
+    return TL_OK;
+}
+
+int check_layer_slot(const tl_attn *h, int layer, int slot, int nseq = 1) {
+    if (layer < 0 || layer >= h->nLayer)
+        return fail(TL_ERR_INVALID, "layer %d out of range [0, %d)", layer, h->nLayer);
+    if (nseq < 1 || slot < 0 || slot + nseq > h->maxBatch)
+        return fail(TL_ERR_INVALID, "slots [%d, %d) out of range [0, %d)", slot, slot + nseq,
+                    h->maxBatch);
+    return TL_OK;
+}
+
+int ensure_io(tl_attn *h, size_t floats) {
+    if (floats <= h->ioCap) return TL_OK;
+    if (h->dIo) cudaFree(h->dIo);
+    h->dIo = nullptr;
+    h->ioCap = 0;
+    size_t cap = std::max<size_t>(floats, 1 << 16);
+    TL_CUDA(cudaMalloc(&h->dIo, cap * sizeof(float)));
+    h->ioCap = cap;
+    return TL_OK;
+}
+
+int ensure_partial(tl_attn *h, size_t floats) {
+    if (floats <= h->partialCap) return TL_OK;
+    if (h->dPartial) {
+        // the old buffer may still be in use by queued work on any stream of this device
+        TL_CUDA(cudaDeviceSynchronize());
+        cudaFree(h->dPartial);
+    }
+    h->dPartial = nullptr;
+    h->partialCap = 0;
+    size_t cap = std::max<size_t>(floats + floats / 4, 1 << 16);
+    TL_CUDA(cudaMalloc(&h->dPartial, cap * sizeof(float)));
+    h->partialCap = cap;
+    return TL_OK;
+}
+
+int ensure_qb(tl_attn *h, size_t bytes) {
+    if (bytes <= h->qbCap) return TL_OK;
+    if (h->dQb) {
+        TL_CUDA(cudaDeviceSynchronize());
+        cudaFree(h->dQb);
+    }
+    h->dQb = nullptr;
+    h->qbCap = 0;
+    TL_CUDA(cudaMalloc(&h->dQb, bytes));
+    h->qbCap = bytes;
+    return TL_OK;
+}
+
+cudaStream_t pick(const tl_attn *h, void *stream) {
+    return stream ? reinterpret_cast<cudaStream_t>(stream) : h->stream;
+}
+
+// Split-KV schedule: chunk length and CTA count for one decode launch.
+struct Plan {
+    int chunk, ctas;
+    size_t partial_floats;
+};
+
+Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset, int slice) {
+    const int G = h->nHead / h->nHeadKv;
+    const int occ = decode_ctas_per_sm(h->headDim, G, h->kvDtype);
+    const int ctas = h->numSms * occ;
+    long long tot = 0;
+    int nmax = 0;
+    std::vector<int> ns(nseq);
+    for (int b = 0; b < nseq; ++b) {
+        int n = slice;
+        if (pos_host) {
+            n = pos_host[b] + 1 - pos_offset;
+            n = std::max(0, std::min(n, slice));
+        }
+        ns[b] = n;
+        tot += n;
+        nmax = std::max(nmax, n);
+    }
+    long long want = (tot * h->nHeadKv + (long long)ctas * 4 - 1) / ((long long)ctas * 4);
+    int chunk = (int)std::min<long long>(1024, std::max<long long>(32, want));
+    chunk = (chunk + 31) / 32 * 32;
+    const int min_chunk = ((nmax + 255) / 256 + 31) / 32 * 32;  // at most 256 chunks/sequence
+    chunk = std::max(chunk, min_chunk);
+    long long units = 0;
+    bool multi = false;
+    for (int b = 0; b < nseq; ++b) {
+        const int nch = ns[b] <= 0 ? 1 : (ns[b] + chunk - 1) / chunk;
+        multi |= nch > 1;
+        units += (long long)nch * h->nHeadKv;
+    }
+    Plan p;
+    p.chunk = chunk;
+    p.ctas = (int)std::max<long long>(1, std::min<long long>(units, ctas));
+    p.partial_floats = multi ? decode_partial_floats((int)units, G, h->headDim) : 0;
+    return p;
+}
+
+int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, const int *pos_host,
+               const float *q, float *out, cudaStream_t s, int pos_offset, float *lse_out) {
+    Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen);
+    TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
+    DecodeArgs a{};
+    a.q = q;
+    a.out = out;
+    a.pos = pos_dev;
+    a.nseq = nseq;
+    a.nHead = h->nHead;
+    a.nHeadKv = h->nHeadKv;
+    a.headDim = h->headDim;
+    a.layer = layer;
+    a.slot0 = slot0;
+    a.pos_offset = pos_offset;
+    a.chunk = p.chunk;
+    a.kv = h->kv;
+    a.partial = h->dPartial;
+    a.partial_cap = h->partialCap;
+    a.counter = h->dCounter + (size_t)slot0 * h->nHeadKv;
+    a.err = h->dErr;
+    a.lse_out = lse_out;
+    cudaError_t e = launch_decode(a, p.ctas, s);
+    if (e == cudaErrorNotSupported) return fail(TL_ERR_UNSUPPORTED, "decode: shape not covered");
+    TL_CUDA(e);
+    return TL_OK;
+}
+
+RopeAppendArgs rope_args(tl_attn *h) {
+    RopeAppendArgs a{};
+    a.kv = h->kv;
+    a.err = h->dErr;
+    return a;
+}
+
+// Synchronise the stream, then read and clear the device error word.
+int finish(tl_attn *h, cudaStream_t s) {
+    unsigned word = 0;
+    TL_CUDA(cudaMemcpyAsync(&word, h->dErr, sizeof word, cudaMemcpyDeviceToHost, s));
+    TL_CUDA(cudaStreamSynchronize(s));
+    if (word) {
+        cudaMemsetAsync(h->dErr, 0, sizeof(unsigned), s);
+        cudaMemsetAsync(h->dCounter, 0, sizeof(unsigned) * (size_t)h->maxBatch * h->nHeadKv, s);
+        cudaStreamSynchronize(s);
+        std::string bits;
+        if (word & TL_DEVERR_POS_RANGE) bits += " position-out-of-range";
+        if (word & TL_DEVERR_TIMEOUT) bits += " wait-timeout";
+        if (word & TL_DEVERR_BAD_ARG) bits += " bad-argument";
+        return fail(TL_ERR_DEVICE, "device error word 0x%x:%s", word, bits.c_str());
+    }
+    return TL_OK;
+}
+
+HeadView col_view(float *p, int H, int D, int S) {
+    // reference column layout [H*D, S]: (h, d, token t) at (h*D + d)*S + t
+    HeadView v{p, 0, 1, (int64_t)D * S, (int64_t)S};
+    (void)H;
+    return v;
+}
+
+HeadView tok_view(float *p, int H, int D, int S) {
+    // token-major [B][S][H*D]
+    HeadView v{p, (int64_t)S * H * D, (int64_t)H * D, (int64_t)D, 1};
+    return v;
+}
+
+int prefill_attention(tl_attn *h, int layer, int slot0, int nseq, int S, HeadView q, HeadView out,
+                      bool qb_ready, bool force_f32, cudaStream_t s) {
+    PrefillArgs a{};
+    a.q = q;
+    a.out = out;
+    a.kf.ptr = nullptr;
+    a.vf.ptr = nullptr;
+    a.pos0 = nullptr;
+    a.nseq = nseq;
+    a.ntok = S;
+    a.nHead = h->nHead;
+    a.nHeadKv = h->nHeadKv;
+    a.headDim = h->headDim;
+    a.layer = layer;
+    a.slot0 = slot0;
+    a.kv = h->kv;
+    a.qb = h->dQb;
+    a.err = h->dErr;
+    if (!force_f32 && qb_ready) {
+        cudaError_t e = launch_prefill_tc(a, s);
+        if (e == cudaSuccess) return TL_OK;
+        if (e != cudaErrorNotSupported) TL_CUDA(e);
+    }
+    cudaError_t e = launch_prefill_f32(a, s);
+    if (e == cudaErrorNotSupported) return fail(TL_ERR_UNSUPPORTED, "prefill: shape not covered");
+    TL_CUDA(e);
+    return TL_OK;
+}
+
+bool tc_prefill_eligible(const tl_attn *h) { return h->kvDtype == TL_KV_BF16 && h->headDim == 64; }
+
+}  // namespace
+
+extern "C" {
+
+const char *tl_last_error(void) { return g_err.c_str(); }
+int tl_version(void) { return TL_ATTN_VERSION; }
+
+int tl_attn_create(tl_attn **out, int nLayer, int nHead, int nHeadKv, int headDim, int ropeDim,
+                   float ropeBase, int maxLen, int maxBatch, int kvDtype, int device) {
+    if (!out) return fail(TL_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    TL_TRY(check_shape(nHead, nHeadKv, headDim));
+    if (ropeDim == 0) ropeDim = headDim;
+    if (ropeDim < 0 || ropeDim > headDim || (ropeDim & 1))
+        return fail(TL_ERR_INVALID, "ropeDim %d must be even and <= headDim %d", ropeDim, headDim);
+    if (nLayer <= 0 || maxLen <= 0 || maxBatch <= 0)
+        return fail(TL_ERR_INVALID, "nLayer, maxLen and maxBatch must be positive");
+    if (kvDtype != TL_KV_F32 && kvDtype != TL_KV_BF16)
+        return fail(TL_ERR_INVALID, "kvDtype %d is neither TL_KV_F32 nor TL_KV_BF16", kvDtype);
+    int ndev = 0;
+    TL_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev)
+        return fail(TL_ERR_INVALID, "device %d out of range [0, %d)", device, ndev);
+    DeviceGuard g(device);
+    tl_attn *h = new tl_attn();
+    h->device = device;
+    h->nLayer = nLayer;
+    h->nHead = nHead;
+    h->nHeadKv = nHeadKv;
+    h->headDim = headDim;
+    h->ropeDim = ropeDim;
+    h->ropeBase = ropeBase;
+    h->maxLen = maxLen;
+    h->maxBatch = maxBatch;
+    h->kvDtype = kvDtype;
+    h->curLen.assign(maxBatch, 0);
+    auto cleanup = [&](int code) {
+        tl_attn_destroy(h);
+        return code;
+    };
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+        return cleanup(fail(TL_ERR_CUDA, "cudaGetDeviceProperties failed"));
+    if (prop.major != 10)
+        return cleanup(fail(TL_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                            device, prop.major, prop.minor));
+    h->numSms = prop.multiProcessorCount;
+    const size_t elems = (size_t)nLayer * maxBatch * nHeadKv * (size_t)maxLen * headDim;
+    const size_t bytes = elems * esize(kvDtype);
+    h->kv.nLayer = nLayer;
+    h->kv.maxBatch = maxBatch;
+    h->kv.nHeadKv = nHeadKv;
+    h->kv.maxLen = maxLen;
+    h->kv.headDim = headDim;
+    h->kv.dtype = kvDtype;
+    cudaError_t e;
+    if ((e = cudaMalloc(&h->kv.k, bytes)) != cudaSuccess ||
+        (e = cudaMalloc(&h->kv.v, bytes)) != cudaSuccess)
+        return cleanup(fail(TL_ERR_NOMEM, "KV cache allocation of 2 x %zu bytes failed: %s", bytes,
+                            cudaGetErrorString(e)));
+    if ((e = cudaMemset(h->kv.k, 0, bytes)) != cudaSuccess ||
+        (e = cudaMemset(h->kv.v, 0, bytes)) != cudaSuccess ||
+        (e = cudaMalloc(&h->dPos, sizeof(int) * (size_t)maxBatch)) != cudaSuccess ||
+        (e = cudaMalloc(&h->dErr, sizeof(unsigned) * 4)) != cudaSuccess ||
+        (e = cudaMemset(h->dErr, 0, sizeof(unsigned) * 4)) != cudaSuccess ||
+        (e = cudaMalloc(&h->dCounter, sizeof(unsigned) * (size_t)maxBatch * nHeadKv)) != cudaSuccess ||
+        (e = cudaMemset(h->dCounter, 0, sizeof(unsigned) * (size_t)maxBatch * nHeadKv)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaDeviceSynchronize()) != cudaSuccess)
+        return cleanup(fail(TL_ERR_CUDA, "handle setup failed: %s", cudaGetErrorString(e)));
+    *out = h;
+    return TL_OK;
+}
+
+void tl_dist_finalize(tl_attn *h);
+
+void tl_attn_destroy(tl_attn *h) {
+    if (!h) return;
+    DeviceGuard g(h->device);
+    tl_dist_finalize(h);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    cudaFree(h->kv.k);
+    cudaFree(h->kv.v);
+    cudaFree(h->dPos);
+    cudaFree(h->dErr);
+    cudaFree(h->dCounter);
+    cudaFree(h->dPartial);
+    cudaFree(h->dIo);
+    cudaFree(h->dQb);
+    cudaFree(h->dGather);
+    if (h->hPinned) cudaFreeHost(h->hPinned);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+}
+
+int tl_kv_get_len(const tl_attn *h, int slot, int *len) {
+    if (!h || !len) return fail(TL_ERR_INVALID, "NULL argument");
+    if (slot < 0 || slot >= h->maxBatch) return fail(TL_ERR_INVALID, "slot %d out of range", slot);
+    *len = h->curLen[slot];
+    return TL_OK;
+}
+
+int tl_kv_set_len(tl_attn *h, int slot, int len) {
+    if (!h) return fail(TL_ERR_INVALID, "NULL handle");
+    if (slot < 0 || slot >= h->maxBatch) return fail(TL_ERR_INVALID, "slot %d out of range", slot);
+    if (len < 0 || len > h->maxLen) return fail(TL_ERR_RANGE, "length %d outside [0, %d]", len, h->maxLen);
+    h->curLen[slot] = len;
+    return TL_OK;
+}
+
+int tl_kv_reset(tl_attn *h) {
+    if (!h) return fail(TL_ERR_INVALID, "NULL handle");
+    DeviceGuard g(h->device);
+    const size_t bytes = (size_t)h->nLayer * h->maxBatch * h->nHeadKv * (size_t)h->maxLen * h->headDim *
+                         esize(h->kvDtype);
+    TL_CUDA(cudaMemsetAsync(h->kv.k, 0, bytes, h->stream));
+    TL_CUDA(cudaMemsetAsync(h->kv.v, 0, bytes, h->stream));
+    TL_CUDA(cudaStreamSynchronize(h->stream));
+    std::fill(h->curLen.begin(), h->curLen.end(), 0);
+    return TL_OK;
+}
+
+int tl_kv_clone(tl_attn *dst, const tl_attn *src) {
+    if (!dst || !src) return fail(TL_ERR_INVALID, "NULL handle");
+    if (dst->nLayer != src->nLayer || dst->maxBatch != src->maxBatch || dst->nHeadKv != src->nHeadKv ||
+        dst->maxLen != src->maxLen || dst->headDim != src->headDim || dst->kvDtype != src->kvDtype)
+        return fail(TL_ERR_INVALID, "cloneCache: handles differ in shape");
+    DeviceGuard g(dst->device);
+    const size_t bytes = (size_t)src->nLayer * src->maxBatch * src->nHeadKv * (size_t)src->maxLen *
+                         src->headDim * esize(src->kvDtype);
+    if (dst->device == src->device) {
+        TL_CUDA(cudaMemcpyAsync(dst->kv.k, src->kv.k, bytes, cudaMemcpyDeviceToDevice, dst->stream));
+        TL_CUDA(cudaMemcpyAsync(dst->kv.v, src->kv.v, bytes, cudaMemcpyDeviceToDevice, dst->stream));
+    } else {
+        TL_CUDA(cudaMemcpyPeerAsync(dst->kv.k, dst->device, src->kv.k, src->device, bytes, dst->stream));
+        TL_CUDA(cudaMemcpyPeerAsync(dst->kv.v, dst->device, src->kv.v, src->device, bytes, dst->stream));
+    }
+    TL_CUDA(cudaStreamSynchronize(dst->stream));
+    dst->curLen = src->curLen;
+    return TL_OK;
+}
+
+int tl_kv_read(tl_attn *h, int layer, int slot, float *k, float *v) {
+    if (!h || !k || !v) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot));
+    DeviceGuard g(h->device);
+    const int D = h->headDim, L = h->maxLen, H = h->nHeadKv;
+    const size_t n = (size_t)H * L * D;
+    const size_t es = esize(h->kvDtype);
+    std::vector<uint8_t> kb(n * es), vb(n * es);
+    const size_t off = (size_t)h->kv.row(layer, slot, 0, 0) * D * es;
+    TL_CUDA(cudaMemcpyAsync(kb.data(), (const uint8_t *)h->kv.k + off, n * es, cudaMemcpyDeviceToHost, h->stream));
+    TL_CUDA(cudaMemcpyAsync(vb.data(), (const uint8_t *)h->kv.v + off, n * es, cudaMemcpyDeviceToHost, h->stream));
+    TL_CUDA(cudaStreamSynchronize(h->stream));
+    auto get = [&](const std::vector<uint8_t> &buf, size_t i) -> float {
+        if (es == 4) {
+            float f;
+            memcpy(&f, buf.data() + i * 4, 4);
+            return f;
+        }
+        uint16_t b16;
+        memcpy(&b16, buf.data() + i * 2, 2);
+        uint32_t u = (uint32_t)b16 << 16;
+        float f;
+        memcpy(&f, &u, 4);
+        return f;
+    };
+    // head-major [H][L][D] -> reference dim-major [H*D, L]
+    for (int hh = 0; hh < H; ++hh)
+        for (int p = 0; p < L; ++p)
+            for (int d = 0; d < D; ++d) {
+                const size_t src = ((size_t)hh * L + p) * D + d;
+                const size_t dst = ((size_t)hh * D + d) * L + p;
+                k[dst] = get(kb, src);
+                v[dst] = get(vb, src);
+            }
+    return TL_OK;
+}
+
+// ---- host tier -------------------------------------------------------------------------------
+
+int tl_rope_single_host(tl_attn *h, float *x, int nHead, int headDim, int ropeDim, float base,
+                        int seqLen) {
+    if (!h || !x) return fail(TL_ERR_INVALID, "NULL argument");
+    if (nHead <= 0 || headDim <= 0 || (headDim & 1) || ropeDim < 0 || ropeDim > headDim ||
+        ropeDim / 2 > kMaxRopePairs || seqLen < 0)
+        return fail(TL_ERR_INVALID, "rope: bad shape");
+    if (seqLen == 0) return TL_OK;
+    DeviceGuard g(h->device);
+    const size_t n = (size_t)nHead * headDim * seqLen;
+    TL_TRY(ensure_io(h, n));
+    TL_CUDA(cudaMemcpyAsync(h->dIo, x, n * 4, cudaMemcpyHostToDevice, h->stream));
+    RopeAppendArgs a = rope_args(h);
+    a.q = col_view(h->dIo, nHead, headDim, seqLen);
+    a.nseq = 1;
+    a.ntok = seqLen;
+    a.nHead = nHead;
+    a.nHeadKv = 1;
+    a.headDim = headDim;
+    a.pos0 = nullptr;
+    a.pos0_scalar = 0;
+    a.rope_q = true;
+    TL_CUDA(launch_rope_append(a, make_rope_tab(ropeDim, base), h->stream));
+    TL_CUDA(cudaMemcpyAsync(x, h->dIo, n * 4, cudaMemcpyDeviceToHost, h->stream));
+    return finish(h, h->stream);
+}
+
+int tl_rope_at_pos_host(tl_attn *h, float *x, int nHead, int headDim, int ropeDim, float base,
+                        int pos, int seqLen) {
+    if (!h || !x) return fail(TL_ERR_INVALID, "NULL argument");
+    if (nHead <= 0 || headDim <= 0 || (headDim & 1) || ropeDim < 0 || ropeDim > headDim ||
+        ropeDim / 2 > kMaxRopePairs || seqLen <= 0)
+        return fail(TL_ERR_INVALID, "rope: bad shape");
+    DeviceGuard g(h->device);
+    const size_t n = (size_t)nHead * headDim * seqLen;
+    TL_TRY(ensure_io(h, n));
+    TL_CUDA(cudaMemcpyAsync(h->dIo, x, n * 4, cudaMemcpyHostToDevice, h->stream));
+    RopeAppendArgs a = rope_args(h);
+    a.q = col_view(h->dIo, nHead, headDim, seqLen);
+    a.q.st = 0;  // only column 0
+    a.nseq = 1;
+    a.ntok = 1;
+    a.nHead = nHead;
+    a.nHeadKv = 1;
+    a.headDim = headDim;
+    a.pos0 = nullptr;
+    a.pos0_scalar = pos;
+    a.rope_q = true;
+    TL_CUDA(launch_rope_append(a, make_rope_tab(ropeDim, base), h->stream));
+    TL_CUDA(cudaMemcpyAsync(x, h->dIo, n * 4, cudaMemcpyDeviceToHost, h->stream));
+    return finish(h, h->stream);
+}
+
+int tl_kv_store_host(tl_attn *h, int layer, int slot, int startPos, const float *k,
+                     const float *v, int cols) {
+    if (!h || !k || !v) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot));
+    if (cols < 0 || startPos < 0) return fail(TL_ERR_INVALID, "storeKVRange: negative position or width");
+    if ((long long)startPos + cols > h->maxLen)
+        return fail(TL_ERR_RANGE, "storeKVRange: columns [%d, %d) exceed maxLen %d", startPos,
+                    startPos + cols, h->maxLen);
+    if (cols == 0) return TL_OK;
+    DeviceGuard g(h->device);
+    const int D = h->headDim, H = h->nHeadKv;
+    const size_t n = (size_t)H * D * cols;
+    TL_TRY(ensure_io(h, 2 * n));
+    TL_CUDA(cudaMemcpyAsync(h->dIo, k, n * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(h->dIo + n, v, n * 4, cudaMemcpyHostToDevice, h->stream));
+    RopeAppendArgs a = rope_args(h);
+    a.k = col_view(h->dIo, H, D, cols);
+    a.v = col_view(h->dIo + n, H, D, cols);
+    a.nseq = 1;
+    a.ntok = cols;
+    a.nHead = h->nHead;
+    a.nHeadKv = H;
+    a.headDim = D;
+    a.pos0_scalar = startPos;
+    a.store = true;
+    a.layer = layer;
+    a.slot0 = slot;
+    TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), h->stream));
+    return finish(h, h->stream);
+}
+
+int tl_attention_full_host(tl_attn *h, const float *q, const float *k, const float *v,
+                           int seqLen, int nHead, int nHeadKv, int headDim, float *ctx) {
+    if (!h || !q || !k || !v || !ctx) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_shape(nHead, nHeadKv, headDim));
+    if (seqLen < 0) return fail(TL_ERR_INVALID, "seqLen < 0");
+    if (seqLen == 0) return TL_OK;
+    DeviceGuard g(h->device);
+    const size_t nq = (size_t)nHead * headDim * seqLen, nk = (size_t)nHeadKv * headDim * seqLen;
+    TL_TRY(ensure_io(h, 2 * nq + 2 * nk));
+    float *dq = h->dIo, *dk = dq + nq, *dv = dk + nk, *dc = dv + nk;
+    TL_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    PrefillArgs a{};
+    a.q = col_view(dq, nHead, headDim, seqLen);
+    a.out = col_view(dc, nHead, headDim, seqLen);
+    a.kf = col_view(dk, nHeadKv, headDim, seqLen);
+    a.vf = col_view(dv, nHeadKv, headDim, seqLen);
+    a.pos0 = nullptr;
+    a.nseq = 1;
+    a.ntok = seqLen;
+    a.nHead = nHead;
+    a.nHeadKv = nHeadKv;
+    a.headDim = headDim;
+    a.kv = h->kv;
+    a.err = h->dErr;
+    cudaError_t e = launch_prefill_f32(a, h->stream);
+    if (e == cudaErrorNotSupported) return fail(TL_ERR_UNSUPPORTED, "attentionFull: shape not covered");
+    TL_CUDA(e);
+    TL_CUDA(cudaMemcpyAsync(ctx, dc, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    return finish(h, h->stream);
+}
+
+int tl_attention_cached_host(tl_attn *h, int layer, int slot, const float *q, int curLen,
+                             int nHead, int nHeadKv, int headDim, float *ctx) {
+    if (!h || !q || !ctx) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot));
+    TL_TRY(check_handle_shape(h, nHead, nHeadKv, headDim));
+    if (curLen < 1 || curLen > h->maxLen)
+        return fail(TL_ERR_RANGE, "attentionCached: curLen %d outside [1, %d]", curLen, h->maxLen);
+    DeviceGuard g(h->device);
+    const size_t nq = (size_t)nHead * headDim;
+    TL_TRY(ensure_io(h, 2 * nq));
+    TL_CUDA(cudaMemcpyAsync(h->dIo, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    const int pos = curLen - 1;
+    TL_CUDA(cudaMemcpyAsync(h->dPos, &pos, sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    TL_TRY(run_decode(h, layer, slot, 1, h->dPos, &pos, h->dIo, h->dIo + nq, h->stream, 0, nullptr));
+    TL_CUDA(cudaMemcpyAsync(ctx, h->dIo + nq, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    return finish(h, h->stream);
+}
+
+int tl_decode_layer_host(tl_attn *h, int layer, int slot, const float *q, const float *k,
+                         const float *v, int pos, float *ctx) {
+    if (!h || !q || !k || !v || !ctx) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot));
+    if (pos >= h->maxLen) return fail(TL_ERR_KV_FULL, "KV cache full");
+    if (pos < 0) return fail(TL_ERR_INVALID, "negative position");
+    return tl_decode_batch_host(h, layer, slot, 1, &pos, q, k, v, ctx);
+}
+
+int tl_decode_batch_host(tl_attn *h, int layer, int slot0, int nseq, const int *pos,
+                         const float *q, const float *k, const float *v, float *out) {
+    if (!h || !pos || !q || !k || !v || !out) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot0, nseq));
+    for (int b = 0; b < nseq; ++b) {
+        if (pos[b] >= h->maxLen) return fail(TL_ERR_KV_FULL, "KV cache full");
+        if (pos[b] < 0) return fail(TL_ERR_INVALID, "negative position");
+    }
+    DeviceGuard g(h->device);
+    const size_t nq = (size_t)nseq * h->nHead * h->headDim, nk = (size_t)nseq * h->nHeadKv * h->headDim;
+    TL_TRY(ensure_io(h, 2 * nq + 2 * nk));
+    float *dq = h->dIo, *dk = dq + nq, *dv = dk + nk, *dout = dv + nk;
+    TL_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(h->dPos, pos, sizeof(int) * nseq, cudaMemcpyHostToDevice, h->stream));
+    TL_TRY(tl_decode_step(h, layer, slot0, nseq, h->dPos, pos, dq, dk, dv, dout, h->stream));
+    TL_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    return finish(h, h->stream);
+}
+
+int tl_prefill_layer_host(tl_attn *h, int layer, int slot, const float *q, const float *k,
+                          const float *v, int seqLen, float *ctx) {
+    if (!h || !q || !k || !v || !ctx) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot));
+    if (seqLen < 0) return fail(TL_ERR_INVALID, "seqLen < 0");
+    if (seqLen > h->maxLen)
+        return fail(TL_ERR_RANGE, "prefill of %d tokens exceeds the KV cache (maxLen %d)", seqLen, h->maxLen);
+    if (seqLen == 0) return TL_OK;
+    DeviceGuard g(h->device);
+    const int D = h->headDim, Hq = h->nHead, Hk = h->nHeadKv;
+    const size_t nq = (size_t)Hq * D * seqLen, nk = (size_t)Hk * D * seqLen;
+    TL_TRY(ensure_io(h, 2 * nq + 2 * nk));
+    float *dq = h->dIo, *dk = dq + nq, *dv = dk + nk, *dc = dv + nk;
+    TL_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    TL_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    const bool tc = tc_prefill_eligible(h);
+    if (tc) TL_TRY(ensure_qb(h, nq * 2));
+    RopeAppendArgs a = rope_args(h);
+    a.q = col_view(dq, Hq, D, seqLen);
+    a.k = col_view(dk, Hk, D, seqLen);
+    a.v = col_view(dv, Hk, D, seqLen);
+    a.nseq = 1;
+    a.ntok = seqLen;
+    a.nHead = Hq;
+    a.nHeadKv = Hk;
+    a.headDim = D;
+    a.pos0_scalar = 0;
+    a.rope_q = a.rope_k = a.store = true;
+    a.layer = layer;
+    a.slot0 = slot;
+    a.qb = tc ? h->dQb : nullptr;
+    TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), h->stream));
+    TL_TRY(prefill_attention(h, layer, slot, 1, seqLen, col_view(dq, Hq, D, seqLen),
+                             col_view(dc, Hq, D, seqLen), tc, false, h->stream));
+    TL_CUDA(cudaMemcpyAsync(ctx, dc, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    return finish(h, h->stream);
+}
+
+// ---- device tier -------------------------------------------------------------------------------
+
+int tl_decode_step(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
+                   const int *pos_host, float *q, float *k, const float *v, float *out,
+                   void *stream) {
+    if (!h || !pos_dev || !q || !k || !v || !out) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot0, nseq));
+    if (pos_host)
+        for (int b = 0; b < nseq; ++b)
+            if (pos_host[b] >= h->maxLen) return fail(TL_ERR_KV_FULL, "KV cache full");
+    DeviceGuard g(h->device);
+    cudaStream_t s = pick(h, stream);
+    const int D = h->headDim;
+    RopeAppendArgs a = rope_args(h);
+    a.q = tok_view(q, h->nHead, D, 1);
+    a.k = tok_view(k, h->nHeadKv, D, 1);
+    a.v = tok_view(const_cast<float *>(v), h->nHeadKv, D, 1);
+    a.nseq = nseq;
+    a.ntok = 1;
+    a.nHead = h->nHead;
+    a.nHeadKv = h->nHeadKv;
+    a.headDim = D;
+    a.pos0 = pos_dev;
+    a.rope_q = a.rope_k = a.store = true;
+    a.layer = layer;
+    a.slot0 = slot0;
+    TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), s));
+    return run_decode(h, layer, slot0, nseq, pos_dev, pos_host, q, out, s, 0, nullptr);
+}
+
+int tl_decode_attention(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
+                        const int *pos_host, const float *q, float *out, void *stream) {
+    if (!h || !pos_dev || !q || !out) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot0, nseq));
+    if (pos_host)
+        for (int b = 0; b < nseq; ++b)
+            if (pos_host[b] >= h->maxLen) return fail(TL_ERR_KV_FULL, "KV cache full");
+    DeviceGuard g(h->device);
+    return run_decode(h, layer, slot0, nseq, pos_dev, pos_host, q, out, pick(h, stream), 0, nullptr);
+}
+
+static int prefill_step_impl(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q,
+                             float *k, const float *v, float *out, void *stream, bool force_f32) {
+    if (!h || !q || !k || !v || !out) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot0, nseq));
+    if (seqLen < 0) return fail(TL_ERR_INVALID, "seqLen < 0");
+    if (seqLen > h->maxLen)
+        return fail(TL_ERR_RANGE, "prefill of %d tokens exceeds the KV cache (maxLen %d)", seqLen, h->maxLen);
+    if (seqLen == 0) return TL_OK;
+    DeviceGuard g(h->device);
+    cudaStream_t s = pick(h, stream);
+    const int D = h->headDim, Hq = h->nHead, Hk = h->nHeadKv;
+    const bool tc = !force_f32 && tc_prefill_eligible(h);
+    if (tc) TL_TRY(ensure_qb(h, (size_t)nseq * Hq * seqLen * D * 2));
+    RopeAppendArgs a = rope_args(h);
+    a.q = tok_view(q, Hq, D, seqLen);
+    a.k = tok_view(k, Hk, D, seqLen);
+    a.v = tok_view(const_cast<float *>(v), Hk, D, seqLen);
+    a.nseq = nseq;
+    a.ntok = seqLen;
+    a.nHead = Hq;
+    a.nHeadKv = Hk;
+    a.headDim = D;
+    a.pos0_scalar = 0;
+    a.rope_q = a.rope_k = a.store = true;
+    a.layer = layer;
+    a.slot0 = slot0;
+    a.qb = tc ? h->dQb : nullptr;
+    TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), s));
+    return prefill_attention(h, layer, slot0, nseq, seqLen, tok_view(q, Hq, D, seqLen),
+                             tok_view(out, Hq, D, seqLen), tc, force_f32, s);
+}
+
+int tl_prefill_step(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q, float *k,
+                    const float *v, float *out, void *stream) {
+    return prefill_step_impl(h, layer, slot0, nseq, seqLen, q, k, v, out, stream, false);
+}
+
+int tl_prefill_step_f32(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q,
+                        float *k, const float *v, float *out, void *stream) {
+    return prefill_step_impl(h, layer, slot0, nseq, seqLen, q, k, v, out, stream, true);
+}
+
+int tl_kv_store(tl_attn *h, int layer, int slot, int startPos, const float *k, const float *v,
+                int cols, void *stream) {
+    if (!h || !k || !v) return fail(TL_ERR_INVALID, "NULL argument");
+    TL_TRY(check_layer_slot(h, layer, slot));
+    if (cols < 0 || startPos < 0) return fail(TL_ERR_INVALID, "storeKVRange: negative position or width");
+    if ((long long)startPos + cols > h->maxLen)
+        return fail(TL_ERR_RANGE, "storeKVRange: columns [%d, %d) exceed maxLen %d", startPos,
+                    startPos + cols, h->maxLen);
+    if (cols == 0) return TL_OK;
+    DeviceGuard g(h->device);
+    RopeAppendArgs a = rope_args(h);
+    a.k = tok_view(const_cast<float *>(k), h->nHeadKv, h->headDim, cols);
+    a.v = tok_view(const_cast<float *>(v), h->nHeadKv, h->headDim, cols);
+    a.nseq = 1;
+    a.ntok = cols;
+    a.nHead = h->nHead;
+    a.nHeadKv = h->nHeadKv;
+    a.headDim = h->headDim;
+    a.pos0_scalar = startPos;
+    a.store = true;
+    a.layer = layer;
+    a.slot0 = slot;
+    TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), pick(h, stream)));
+    return TL_OK;
+}
+
+int tl_check_device(tl_attn *h, void *stream) {
+    if (!h) return fail(TL_ERR_INVALID, "NULL handle");
+    DeviceGuard g(h->device);
+    return finish(h, pick(h, stream));
+}
+
+}  // extern "C"
+
+// Used by dist.cu.
+namespace tl {
+int api_run_decode_lse(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
+                       const int *pos_host, const float *q, float *lse_out, cudaStream_t s,
+                       int pos_offset) {
+    return run_decode(h, layer, slot0, nseq, pos_dev, pos_host, q, nullptr, s, pos_offset, lse_out);
+}
+int api_fail(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace tl
