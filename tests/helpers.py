@@ -33,3 +33,14 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
     u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
     u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
     return u.astype(np.uint32).view(np.float32)
+
+
+def parity(got: np.ndarray, oracle_out: np.ndarray, exact: np.ndarray | None, tol: float) -> tuple[float, float]:
+    """Return (error vs the oracle, allowed).  The allowance is `tol`, plus -- when the float64
+    ground truth `exact` is given -- the oracle's own distance from it: the oracle sums in
+    float32 in sequential order, so over thousands of positions its own rounding is of the
+    order of the bound, and a kernel that sums in a different order is judged against the
+    oracle up to that amount."""
+    err = max_rel_err(got, oracle_out)
+    allowed = tol + (max_rel_err(oracle_out, exact) if exact is not None else 0.0)
+    return err, allowed

@@ -8,7 +8,8 @@ import numpy as np
 import pytest
 
 from oracle import oracle as ora
-from tests.helpers import TOL_BF16, TOL_F32, bf16_round, max_rel_err, randn
+from tests import numpy_ref
+from tests.helpers import TOL_BF16, TOL_F32, bf16_round, max_rel_err, parity, randn
 
 pytestmark = pytest.mark.gpu
 
@@ -80,7 +81,9 @@ def test_decode_step_batched(env, kvd, Hq, Hkv, D, lens):
             kc[:, L:] = kr if kvd == 0 else bf16_round(kr)
             vc[:, L:] = v[b].reshape(-1, 1) if kvd == 0 else bf16_round(v[b].reshape(-1, 1))
             ref = ora.attention_cached(qr, kc, vc, L + 1, Hq, Hkv, D)
-            assert max_rel_err(got[b].reshape(-1, 1), ref) <= TOL_F32, (b, L, max_rel_err(got[b].reshape(-1, 1), ref))
+            exact = numpy_ref.attention(qr, kc, vc, Hq, Hkv, D, np.array([L]), L + 1) if L >= 1024 else None
+            err, allowed = parity(got[b].reshape(-1, 1), ref, exact, TOL_F32)
+            assert err <= allowed, (b, L, err, allowed)
         # repeated calls give identical results (counters are reset by the merging CTA)
         out2 = torch.empty_like(out)
         dq2, dk2 = (torch.from_numpy(a).cuda() for a in (q, k))
