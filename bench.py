@@ -310,7 +310,7 @@ def cpu_decode_sample(lens, Hq, Hkv, D, base, budget_s: float, threads: int, see
 def run_decode_batched(args, dist, kvd: int):
     import torch
     pk = peaks()
-    w = DecodeBatched(kvd, dist.rank)
+    w = DecodeBatched(kvd, dist.rank, B=args.seqs)
     sampler = ClockSampler(dist.local)
     sampler.start()
     ms = time_steps(w.step, args.steps, args.warmup, w.stream, dist)
@@ -394,6 +394,7 @@ def main():
                     choices=["decode_batched", "decode_batched_bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (256 = the benchmark)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     dist = Dist()

@@ -44,3 +44,19 @@ def parity(got: np.ndarray, oracle_out: np.ndarray, exact: np.ndarray | None, to
     err = max_rel_err(got, oracle_out)
     allowed = tol + (max_rel_err(oracle_out, exact) if exact is not None else 0.0)
     return err, allowed
+
+
+def rope_agrees(y: np.ndarray, ref: np.ndarray) -> tuple[float, int]:
+    """RoPE on the device uses the reference's float32 angle and rounding-exact products; only
+    the last bit of cos/sin may differ between glibc and the device.  Returns (fraction of
+    bit-identical elements, max difference in ulps of the reference value)."""
+    y = np.asarray(y, np.float32)
+    ref = np.asarray(ref, np.float32)
+    same = float(np.mean(y == ref))
+    ulps = np.abs(y.astype(np.float64) - ref) / np.spacing(np.maximum(np.abs(ref), np.float32(1e-30)))
+    return same, int(np.max(ulps))
+
+
+def check_rope(y: np.ndarray, ref: np.ndarray) -> None:
+    same, ulps = rope_agrees(y, ref)
+    assert ulps <= 4 and same >= 0.95, (same, ulps)

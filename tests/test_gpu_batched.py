@@ -9,7 +9,7 @@ import pytest
 
 from oracle import oracle as ora
 from tests import numpy_ref
-from tests.helpers import TOL_BF16, TOL_F32, bf16_round, max_rel_err, parity, randn
+from tests.helpers import TOL_BF16, TOL_F32, bf16_round, max_rel_err, normwise_err, parity, randn
 
 pytestmark = pytest.mark.gpu
 
@@ -165,8 +165,15 @@ def test_prefill_step_batched(env, kvd, S):
             qr = ora.rope_single(qc, Hq, D, D, 10000.0)
             kr = ora.rope_single(kc, Hkv, D, D, 10000.0)
             ref = ora.attention_full_ctx(qr, kr, vc, Hq, Hkv, D)
-            err = max_rel_err(np.ascontiguousarray(got[b].T), ref)
-            assert err <= tol, (b, err)
+            g = np.ascontiguousarray(got[b].T)
+            if kvd == 0:
+                err = max_rel_err(g, ref)
+                assert err <= TOL_F32, (b, err)
+            else:
+                # bf16 tensor-core path (see test_prefill_layer_matches_oracle_step)
+                assert normwise_err(g, ref) <= TOL_BF16, (b, normwise_err(g, ref))
+                ref_b = ora.attention_full_ctx(bf16_round(qr), bf16_round(kr), bf16_round(vc), Hq, Hkv, D)
+                assert normwise_err(g, ref_b) <= 5e-3, (b, normwise_err(g, ref_b))
     finally:
         _lib.lib.tl_attn_destroy(h)
 

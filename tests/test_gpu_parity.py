@@ -11,7 +11,8 @@ import pytest
 
 from oracle import oracle as ora
 from tests import numpy_ref
-from tests.helpers import TOL_BF16, TOL_F32, bf16_round, max_rel_err, parity, randn
+from tests.helpers import (TOL_BF16, TOL_F32, bf16_round, check_rope, max_rel_err, normwise_err,
+                           parity, randn)
 
 pytestmark = pytest.mark.gpu
 
@@ -32,13 +33,12 @@ def hp(fa, **kw):
 
 # ---- RoPE ---------------------------------------------------------------------------------
 
-def test_apply_rope_single_bit_exact(fa):
+def test_apply_rope_single(fa):
     rng = np.random.default_rng(10)
     x = randn(rng, 32 * 64, 8)
     y = x.copy()
     fa.applyRopeSingle(y, 32, 64, 64, 10000.0)
-    ref = ora.rope_single(x, 32, 64, 64, 10000.0)
-    assert np.array_equal(y, ref), float(np.max(np.abs(y - ref)))
+    check_rope(y, ora.rope_single(x, 32, 64, 64, 10000.0))
 
 
 @pytest.mark.parametrize("pos,base", [(0, 10000.0), (37, 10000.0), (4095, 10000.0), (131071, 500000.0)])
@@ -51,7 +51,7 @@ def test_apply_rope_at_pos(fa, pos, base):
     # column 0 rotated, other columns untouched; the angles are the same float32 products, so
     # only a last-bit difference between glibc's and the device's cos/sin can remain
     assert np.array_equal(y[:, 1:], x[:, 1:])
-    assert np.max(np.abs(y - ref)) <= 4 * np.max(np.spacing(np.abs(ref)))
+    check_rope(y, ref)
 
 
 def test_rope_partial_ropedim(fa):
@@ -59,7 +59,8 @@ def test_rope_partial_ropedim(fa):
     x = randn(rng, 4 * 64, 5)
     y = x.copy()
     fa.applyRopeSingle(y, 4, 64, 32, 10000.0)
-    assert np.array_equal(y, ora.rope_single(x, 4, 64, 32, 10000.0))
+    check_rope(y, ora.rope_single(x, 4, 64, 32, 10000.0))
+    assert np.array_equal(y.reshape(4, 64, 5)[:, 32:], x.reshape(4, 64, 5)[:, 32:])
 
 
 # ---- storeKVRange / KvCache ---------------------------------------------------------------
@@ -204,13 +205,17 @@ def test_prefill_layer_matches_oracle_step(fa, S, kvd):
     ctx = fa.prefillLayer(cache, 0, q, k, v)
     qr = ora.rope_single(q, 32, 64, 64, 10000.0)
     kr = ora.rope_single(k, 4, 64, 64, 10000.0)
+    ref = ora.attention_full_ctx(qr, kr, v, 32, 4, 64)
     if kvd == 0:
-        ref = ora.attention_full_ctx(qr, kr, v, 32, 4, 64)
         assert max_rel_err(ctx, ref) <= TOL_F32
-        assert np.array_equal(cache.k[0][:, :S], kr)
+        check_rope(cache.k[0][:, :S], kr)
     else:
-        ref = ora.attention_full_ctx(qr, kr, v, 32, 4, 64)
-        assert max_rel_err(ctx, ref) <= TOL_BF16, max_rel_err(ctx, ref)
+        # bf16 tensor-core path: Q, K, V and P are bf16, so entries near zero carry an absolute
+        # error of a few 1e-3; the bound is normwise against the fp32 oracle, and tighter
+        # against the oracle fed the same bf16-rounded inputs
+        assert normwise_err(ctx, ref) <= TOL_BF16, normwise_err(ctx, ref)
+        ref_b = ora.attention_full_ctx(bf16_round(qr), bf16_round(kr), bf16_round(v), 32, 4, 64)
+        assert normwise_err(ctx, ref_b) <= 5e-3, normwise_err(ctx, ref_b)
 
 
 def test_prefill_overflow_is_refused(fa):

@@ -7,10 +7,12 @@
 // in the log2 domain -- into its own slot of a gather buffer; one in-place ncclAllGather
 // exchanges the slots (B*nHead*(headDim+2) floats per rank) and a merge kernel combines them:
 //   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L.
+#include <dlfcn.h>
 #include <nccl.h>
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "internal.h"
 
@@ -24,11 +26,48 @@ int api_fail(int code, const char *msg);
 using namespace tl;
 
 namespace {
+
+// NCCL is resolved at first use with dlopen, not linked: the library then loads in processes
+// that never use the multi-GPU calls, and a host that has already loaded an NCCL (PyTorch
+// does) keeps using that one instead of a second copy with the same soname.
+struct Nccl {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *);
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    const char *(*GetErrorString)(ncclResult_t);
+    bool ok;
+};
+
+const Nccl &nccl() {
+    static Nccl n{};
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        n.GetUniqueId = reinterpret_cast<decltype(n.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+        n.CommInitRank = reinterpret_cast<decltype(n.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+        n.AllGather = reinterpret_cast<decltype(n.AllGather)>(dlsym(h, "ncclAllGather"));
+        n.CommDestroy = reinterpret_cast<decltype(n.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        n.GetErrorString = reinterpret_cast<decltype(n.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+        n.ok = n.GetUniqueId && n.CommInitRank && n.AllGather && n.CommDestroy && n.GetErrorString;
+    });
+    return n;
+}
+
 int nccl_fail(ncclResult_t r, const char *what) {
     char buf[256];
-    snprintf(buf, sizeof buf, "%s: %s", what, ncclGetErrorString(r));
+    snprintf(buf, sizeof buf, "%s: %s", what, nccl().ok ? nccl().GetErrorString(r) : "NCCL unavailable");
     return api_fail(TL_ERR_NCCL, buf);
 }
+
+#define TL_NEED_NCCL()                                                                   \
+    do {                                                                                 \
+        if (!nccl().ok) return api_fail(TL_ERR_NCCL, "libnccl.so.2 could not be loaded"); \
+    } while (0)
+
 }  // namespace
 
 extern "C" {
@@ -36,8 +75,9 @@ extern "C" {
 int tl_dist_unique_id(char *id128) {
     if (!id128) return api_fail(TL_ERR_INVALID, "NULL id buffer");
     static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    TL_NEED_NCCL();
     ncclUniqueId id;
-    ncclResult_t r = ncclGetUniqueId(&id);
+    ncclResult_t r = nccl().GetUniqueId(&id);
     if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
     memcpy(id128, &id, sizeof id);
     return TL_OK;
@@ -47,13 +87,14 @@ int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank) {
     if (!h || !id128) return api_fail(TL_ERR_INVALID, "NULL argument");
     if (nranks < 1 || rank < 0 || rank >= nranks) return api_fail(TL_ERR_INVALID, "bad rank/nranks");
     if (h->comm) return api_fail(TL_ERR_INVALID, "handle already joined a communicator");
+    TL_NEED_NCCL();
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     ncclUniqueId id;
     memcpy(&id, id128, sizeof id);
     ncclComm_t comm;
-    ncclResult_t r = ncclCommInitRank(&comm, nranks, id, rank);
+    ncclResult_t r = nccl().CommInitRank(&comm, nranks, id, rank);
     cudaSetDevice(prev);
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
     h->comm = comm;
@@ -68,7 +109,7 @@ void tl_dist_finalize(tl_attn *h) {
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     if (h->stream) cudaStreamSynchronize(h->stream);
-    ncclCommDestroy(reinterpret_cast<ncclComm_t>(h->comm));
+    nccl().CommDestroy(reinterpret_cast<ncclComm_t>(h->comm));
     cudaSetDevice(prev);
     h->comm = nullptr;
     h->nranks = 1;
@@ -108,7 +149,7 @@ int tl_decode_attention_dist(tl_attn *h, int layer, int slot0, int nseq, const i
     rc = api_run_decode_lse(h, layer, slot0, nseq, pos_dev, pos_host, q, mine, s,
                             h->rank * h->maxLen);
     if (rc == TL_OK) {
-        ncclResult_t r = ncclAllGather(mine, h->dGather, per_rank, ncclFloat,
+        ncclResult_t r = nccl().AllGather(mine, h->dGather, per_rank, ncclFloat,
                                        reinterpret_cast<ncclComm_t>(h->comm), s);
         if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather");
     }
