@@ -46,17 +46,19 @@ def parity(got: np.ndarray, oracle_out: np.ndarray, exact: np.ndarray | None, to
     return err, allowed
 
 
-def rope_agrees(y: np.ndarray, ref: np.ndarray) -> tuple[float, int]:
+def rope_agrees(y: np.ndarray, ref: np.ndarray) -> tuple[float, float]:
     """RoPE on the device uses the reference's float32 angle and rounding-exact products; only
-    the last bit of cos/sin may differ between glibc and the device.  Returns (fraction of
-    bit-identical elements, max difference in ulps of the reference value)."""
+    the last bit of cos/sin may differ between glibc and the device.  A rotated value that
+    cancels to near zero (x0*c - x1*s) turns that into many ulps of itself, so the difference
+    is measured in ulps of the largest value.  Returns (fraction of bit-identical elements,
+    max |difference| in ulps of max |ref|)."""
     y = np.asarray(y, np.float32)
     ref = np.asarray(ref, np.float32)
     same = float(np.mean(y == ref))
-    ulps = np.abs(y.astype(np.float64) - ref) / np.spacing(np.maximum(np.abs(ref), np.float32(1e-30)))
-    return same, int(np.max(ulps))
+    ulp = float(np.spacing(np.float32(np.max(np.abs(ref)))))
+    return same, float(np.max(np.abs(y.astype(np.float64) - ref)) / ulp)
 
 
 def check_rope(y: np.ndarray, ref: np.ndarray) -> None:
     same, ulps = rope_agrees(y, ref)
-    assert ulps <= 4 and same >= 0.95, (same, ulps)
+    assert ulps <= 2 and same >= 0.98, (same, ulps)
