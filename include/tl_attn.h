@@ -168,6 +168,26 @@ TL_API int tl_kv_store(tl_attn *h, int layer, int slot, int startPos, const floa
  * TL_ERR_DEVICE (message names the bits). */
 TL_API int tl_check_device(tl_attn *h, void *stream);
 
+/* ---- allocation-free decode ------------------------------------------------------------- */
+
+/* No counterpart in the reference.  For callers that cannot allocate device memory (a host
+ * whose allocator owns all of it, code running under CUDA graph capture, a loop that must not
+ * take an allocation's latency): the same split-KV decode attention as tl_decode_attention,
+ * without a handle and without any allocation.  The caller passes q [nseq][nHead*headDim],
+ * the cache K and V, each head-major [nseq][nHeadKv][maxLen][headDim] of f32 or bf16 with
+ * RoPE already applied, positions pos_dev / pos_host (both required; sequence b attends
+ * positions 0..pos[b]) and out [nseq][nHead*headDim], all on the current device; the call is
+ * asynchronous on `stream`.  The kernel's scratch is a fixed 16 MiB array inside the
+ * library, held by every GPU that loads it until exit: at most 65536 (sequence, kv-head)
+ * pairs per call, larger calls are refused with TL_ERR_INVALID.  The first call on a device
+ * looks the array up (cudaGetSymbolAddress) and should come before any stream capture.  All
+ * calls share the array and clear what they use at their start, so calls that can overlap
+ * on the GPU race and must not be issued. */
+TL_API int tl_decode_attention_noalloc(const float *q, const void *k_cache, const void *v_cache,
+                                       int kvDtype, int nHead, int nHeadKv, int headDim, int maxLen,
+                                       int nseq, const int *pos_dev, const int *pos_host, float *out,
+                                       void *stream);
+
 /* ---- multi-GPU split-KV (one process per GPU, NCCL over NVLink) ---------------------------- */
 
 /* NCCL unique id (128 bytes) created on one rank and shared with the others by the caller. */

@@ -56,6 +56,7 @@ SIGNATURES = {
     "tl_prefill_step_f32": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "tl_kv_store": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
     "tl_check_device": (_I, [_P, _P]),
+    "tl_decode_attention_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "tl_dist_unique_id": (_I, [_P]),
     "tl_dist_init": (_I, [_P, _P, _I, _I]),
     "tl_decode_attention_dist": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
