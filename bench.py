@@ -343,6 +343,8 @@ def run_decode_batched(args, dist, kvd: int):
                      "algorithmic_bytes_per_launch": w.algorithmic_bytes_attention(),
                      "launch_ms": round(ms_attn, 4)},
     }
+    if not args.no_prefill:
+        res["prefill"] = run_prefill(args, dist)
     if n == 1 and dist.rank == 0 and not args.no_cpu_baseline:
         rate, sample = cpu_decode_sample(w.lens, w.Hq, w.Hkv, w.D, w.base, args.cpu_budget, 1)
         res["cpu_baseline"] = {"value": round(rate, 3), "unit": "tok/s", "cores": 1, "kind": "port",
@@ -350,6 +352,120 @@ def run_decode_batched(args, dist, kvd: int):
                                                   "Malebolgia path, src/forward.nim:51-74)"}
     w.close()
     return res
+
+
+# -------------------------------------------------------------------- prefill (tcgen05)
+def prefill_point(S: int, steps: int, warmup: int, B=8, Hq=32, Hkv=8, D=64, kvd=1):
+    """Causal prefill of B sequences of S tokens: RoPE + bf16 cache write + attention
+    (tl_prefill_step).  Returns (ms per step, TFLOP/s of the attention, flops)."""
+    import torch
+    from tinylama_b200 import _lib
+    h = C.c_void_p()
+    _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, 10000.0, S, B, kvd,
+                                       torch.cuda.current_device()))
+    try:
+        stream = torch.cuda.Stream()
+        torch.cuda.set_stream(stream)
+        g = torch.Generator(device="cuda").manual_seed(S)
+        q = torch.randn(B, S, Hq * D, device="cuda", generator=g)
+        k = torch.randn(B, S, Hkv * D, device="cuda", generator=g)
+        v = torch.randn(B, S, Hkv * D, device="cuda", generator=g)
+        out = torch.empty_like(q)
+        p = lambda t: C.c_void_p(t.data_ptr())
+        sp = C.c_void_p(stream.cuda_stream)
+
+        def step():
+            _lib.check(_lib.lib.tl_prefill_step(h, 0, 0, B, S, p(q), p(k), p(v), p(out), sp))
+
+        class _D:
+            def barrier(self): pass
+            def max(self, x): return x
+        ms = time_steps(step, steps, warmup, stream, _D())
+        _lib.check(_lib.lib.tl_check_device(h, C.c_void_p(stream.cuda_stream)))
+        flops = B * Hq * 2 * D * S * (S + 1)
+        return ms, flops / (ms / 1e3) / 1e12, flops
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
+def run_prefill(args, dist, sizes=(512, 2048, 8192)):
+    pk = peaks()
+    res = {}
+    for S in sizes:
+        ms, tf, flops = prefill_point(S, max(5, args.steps // 2), args.warmup)
+        res[str(S)] = {"ms_per_step": round(ms, 4), "tflops": round(tf, 1),
+                       "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4), "flops": flops}
+    return {"workload": "causal prefill, 8 sequences, 32 q / 8 kv heads, head_dim 64, bf16 KV "
+                        "(tcgen05), step = RoPE + cache write + attention",
+            "by_seq_len": res, "peak_tflops": pk["bf16_tflops"], "peak_src": pk["src"]}
+
+
+# ------------------------------------------------------------ long-context split-KV decode
+def run_splitkv(args, dist, B=4, Hq=32, Hkv=8, D=128, L=131072, base=500000.0):
+    """One 131072-token context per sequence, split along the sequence axis: rank r holds
+    positions [r*L/N, (r+1)*L/N).  A step is the split-KV attention of one query token per
+    sequence at position L-1 (tl_decode_attention_dist: local partials, NCCL all-gather of the
+    (m, l, o) partials, merge).  Strong scaling: the total work is fixed."""
+    import torch
+    from tinylama_b200 import _lib
+    n, r = dist.world, dist.rank
+    assert L % n == 0
+    slice_len = L // n
+    h = C.c_void_p()
+    _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, base, slice_len, B, 1,
+                                       torch.cuda.current_device()))
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = C.c_void_p(stream.cuda_stream)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    try:
+        g = torch.Generator(device="cuda").manual_seed(900 + r)
+        for b in range(B):
+            k = torch.randn(slice_len, Hkv * D, device="cuda", generator=g)
+            v = torch.randn(slice_len, Hkv * D, device="cuda", generator=g)
+            _lib.check(_lib.lib.tl_kv_store(h, 0, b, 0, p(k), p(v), slice_len, sp))
+            del k, v
+        uid = C.create_string_buffer(128)
+        if r == 0:
+            _lib.check(_lib.lib.tl_dist_unique_id(uid))
+        if n > 1:
+            obj = [uid.raw if r == 0 else None]
+            dist.pg.broadcast_object_list(obj, src=0)
+            uid = C.create_string_buffer(obj[0], 128)
+        _lib.check(_lib.lib.tl_dist_init(h, uid, n, r))
+        gq = torch.Generator(device="cuda").manual_seed(4242)  # same q on every rank
+        q = torch.randn(B, Hq * D, device="cuda", generator=gq)
+        out = torch.empty(B, Hq * D, device="cuda")
+        pos_host = np.full(B, L - 1, np.int32)
+        pos = torch.from_numpy(pos_host).cuda()
+        torch.cuda.synchronize()
+
+        def step():
+            _lib.check(_lib.lib.tl_decode_attention_dist(h, 0, 0, B, p(pos), pos_host.ctypes.data_as(C.c_void_p),
+                                                         p(q), p(out), sp))
+
+        ms = time_steps(step, args.steps, args.warmup, stream, dist)
+        _lib.check(_lib.lib.tl_check_device(h, sp))
+        kv_bytes = B * L * Hkv * D * 2 * 2
+        pk = peaks()
+        gbs = kv_bytes / (ms / 1e3) / 1e9
+        return {
+            "metric": "long-context split-KV decode attn tok/s", "value": round(B / (ms / 1e3), 1),
+            "unit": "tok/s", "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16-kv/f32-math", "data": "synthetic",
+            "config": {"workload": "long-context split-KV decode (Llama-3-8B-style attention)",
+                       "batch": B, "ctx_len": L, "n_head": Hq, "n_head_kv": Hkv, "head_dim": D,
+                       "rope_theta": base, "kv_dtype": "bf16", "parallelism": f"split-KV x{n} + NCCL all-gather merge",
+                       "l2": f"no flush: {kv_bytes / n / 1e9:.2f} GB of KV per GPU per step > 126 MB L2"},
+            "hbm_gbs_aggregate": round(gbs, 1), "hbm_gbs_per_gpu": round(gbs / n, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs / n, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / n / pk["hbm_gbs"], 4), "peak_src": pk["src"],
+                         "note": "per GPU, whole step (local attention + all-gather + merge)"},
+            "gpu_launches": 2 * args.steps,
+        }
+    finally:
+        _lib.lib.tl_attn_destroy(h)
 
 
 def run_reference(args, dist):
@@ -391,8 +507,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_batched",
-                    choices=["decode_batched", "decode_batched_bf16"])
+                    choices=["decode_batched", "decode_batched_bf16", "splitkv", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="omit the prefill sub-measurement")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (256 = the benchmark)")
     args = ap.parse_args()
@@ -407,8 +524,12 @@ def main():
     try:
         if args.workload == "decode_batched":
             res = run_decode_batched(args, dist, 0)
-        else:
+        elif args.workload == "decode_batched_bf16":
             res = run_decode_batched(args, dist, 1)
+        elif args.workload == "splitkv":
+            res = run_splitkv(args, dist)
+        else:
+            res = run_prefill(args, dist)
         if dist.rank == 0:
             print(json.dumps(res), flush=True)
     finally:

@@ -1,0 +1,99 @@
+"""Split-KV decode across two GPUs (tl_decode_attention_dist over NCCL) against the single-GPU
+decode over the whole context, on two B200s.  One process per GPU, spawned; the NCCL id is
+created in the parent and passed to both."""
+import ctypes as C
+import multiprocessing as mp
+import os
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _ngpus() -> int:
+    import torch
+    return torch.cuda.device_count()
+
+
+def _worker(rank, nranks, uid, kvd, L, out_q):
+    sys.path.insert(0, ROOT)
+    import torch
+    from tinylama_b200 import _lib
+    torch.cuda.set_device(rank)
+    B, Hq, Hkv, D = 2, 32, 8, 128
+    sl = L // nranks
+    rng = np.random.default_rng(7 + kvd)
+    k = rng.standard_normal((B, L, Hkv * D), dtype=np.float32)
+    v = rng.standard_normal((B, L, Hkv * D), dtype=np.float32)
+    q = rng.standard_normal((B, Hq * D), dtype=np.float32)
+    lens = [L - 1, L // 2 - 3]  # the second sequence ends inside rank 0's slice
+    p = lambda t: C.c_void_p(t.data_ptr())
+    h = C.c_void_p()
+    _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, 500000.0, sl, B, kvd, rank))
+    try:
+        for b in range(B):
+            kk = torch.from_numpy(np.ascontiguousarray(k[b, rank * sl:(rank + 1) * sl])).cuda()
+            vv = torch.from_numpy(np.ascontiguousarray(v[b, rank * sl:(rank + 1) * sl])).cuda()
+            _lib.check(_lib.lib.tl_kv_store(h, 0, b, 0, p(kk), p(vv), sl, None))
+        _lib.check(_lib.lib.tl_dist_init(h, C.create_string_buffer(uid, 128), nranks, rank))
+        pos = np.array(lens, np.int32)
+        dpos = torch.from_numpy(pos).cuda()
+        dq = torch.from_numpy(q).cuda()
+        out = torch.empty(B, Hq * D, device="cuda")
+        _lib.check(_lib.lib.tl_decode_attention_dist(h, 0, 0, B, p(dpos), pos.ctypes.data_as(C.c_void_p),
+                                                     p(dq), p(out), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+        got = out.cpu().numpy()
+        ref = None
+        if rank == 0:  # whole context on one GPU
+            h1 = C.c_void_p()
+            _lib.check(_lib.lib.tl_attn_create(C.byref(h1), 1, Hq, Hkv, D, D, 500000.0, L, B, kvd, rank))
+            for b in range(B):
+                kk = torch.from_numpy(np.ascontiguousarray(k[b])).cuda()
+                vv = torch.from_numpy(np.ascontiguousarray(v[b])).cuda()
+                _lib.check(_lib.lib.tl_kv_store(h1, 0, b, 0, p(kk), p(vv), L, None))
+            o1 = torch.empty(B, Hq * D, device="cuda")
+            _lib.check(_lib.lib.tl_decode_attention(h1, 0, 0, B, p(dpos), pos.ctypes.data_as(C.c_void_p),
+                                                    p(dq), p(o1), None))
+            _lib.check(_lib.lib.tl_check_device(h1, None))
+            ref = o1.cpu().numpy()
+            _lib.lib.tl_attn_destroy(h1)
+        out_q.put((rank, got, ref, None))
+    except Exception as e:  # report, never hang the parent
+        out_q.put((rank, None, None, repr(e)))
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
+@pytest.mark.parametrize("kvd", [0, 1])
+def test_splitkv_two_gpus_matches_one(cuda_lib, kvd):
+    if _ngpus() < 2:
+        pytest.skip("needs two GPUs")
+    _lib = cuda_lib
+    uid = C.create_string_buffer(128)
+    _lib.check(_lib.lib.tl_dist_unique_id(uid))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    os.environ.update(env)
+    procs = [ctx.Process(target=_worker, args=(r, 2, uid.raw, kvd, 8192, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, got, ref, err = q.get(timeout=180)
+            assert err is None, (rank, err)
+            results[rank] = (got, ref)
+    finally:
+        for pr in procs:
+            pr.join(timeout=60)
+            if pr.is_alive():
+                pr.kill()
+    ref = results[0][1]
+    for rank in (0, 1):
+        got = results[rank][0]
+        assert np.allclose(got, ref, rtol=1e-4, atol=1e-5), (rank, float(np.max(np.abs(got - ref))))
