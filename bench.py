@@ -388,7 +388,8 @@ def prefill_point(S: int, steps: int, warmup: int, B=8, Hq=32, Hkv=8, D=64, kvd=
         _lib.lib.tl_attn_destroy(h)
 
 
-def run_prefill(args, dist, sizes=(512, 2048, 8192)):
+def run_prefill(args, dist):
+    sizes = [int(x) for x in args.prefill_sizes.split(",")]
     pk = peaks()
     res = {}
     for S in sizes:
@@ -510,6 +511,7 @@ def main():
                     choices=["decode_batched", "decode_batched_bf16", "splitkv", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the prefill sub-measurement")
+    ap.add_argument("--prefill-sizes", default="512,2048,8192", help="sequence lengths of the prefill")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (256 = the benchmark)")
     args = ap.parse_args()

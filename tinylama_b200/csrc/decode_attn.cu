@@ -41,7 +41,9 @@ struct DecCfg {
     static constexpr int THREADS = 32 * (NW + 1);
     static constexpr int TILE_BYTES = T * D * (int)sizeof(KV);
     static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-    static constexpr int NS_RAW = 98304 / STAGE_BYTES;
+    // bytes in flight per CTA: 96 KB for f32 KV (2 CTAs/SM), 48 KB for bf16 KV, whose GQA
+    // consumers need more warps per SM to hide latency (3 CTAs/SM)
+    static constexpr int NS_RAW = (sizeof(KV) == 2 ? 49152 : 98304) / STAGE_BYTES;
     static constexpr int NS = NS_RAW < 2 ? 2 : (NS_RAW > 8 ? 8 : NS_RAW);
     // shared memory carve-up (bytes, all 16-aligned)
     static constexpr int OFF_STAGES = 0;
@@ -269,7 +271,9 @@ decode_kernel(const DecodeArgs a) {
         bool ok = true;
         for (int p = un.p0; p < un.p1; p += C::T) {
             const int np = min(C::T, un.p1 - p);
-            if (!mbar_wait(&full[stage], phase, err, abort_flag)) { ok = false; break; }
+            // warp-uniform verdict, so that the warp's shuffles and barriers stay converged
+            ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, err, abort_flag));
+            if (!ok) break;
             const KV *ks = reinterpret_cast<const KV *>(smem + C::OFF_STAGES + stage * C::STAGE_BYTES);
             const KV *vs = reinterpret_cast<const KV *>(smem + C::OFF_STAGES + stage * C::STAGE_BYTES + C::TILE_BYTES);
             const int jb = warp * C::PPW;
@@ -288,40 +292,60 @@ decode_kernel(const DecodeArgs a) {
                 }
             }
             butterfly<C::NV>(part, lane);
-            {
-                const int base = butterfly_index<C::NV>(lane);
-                constexpr int R = C::NV >= 32 ? C::NV / 32 : 1;
+            constexpr int R = C::NV >= 32 ? C::NV / 32 : 1;
+            const int base = butterfly_index<C::NV>(lane);
+            // owners publish their scores, masking positions past the end of the tile
+            float own[R];
 #pragma unroll
-                for (int r = 0; r < R; ++r) sc[warp * C::NV + base + r] = part[r];
+            for (int r = 0; r < R; ++r) {
+                const int idx = base + r;
+                own[r] = (jb + idx % C::PPW < np) ? part[r] : -INFINITY;
+                sc[warp * C::NV + idx] = own[r];
+            }
+            __syncwarp();
+            // per-head tile maximum (every lane reads the G*PPW scores)
+            float mnew[G];
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                float tmax = -INFINITY;
+#pragma unroll
+                for (int jj = 0; jj < C::PPW; jj += 4) {
+                    const float4 t4 = *reinterpret_cast<const float4 *>(&sc[warp * C::NV + h * C::PPW + jj]);
+                    tmax = fmaxf(tmax, fmaxf(fmaxf(t4.x, t4.y), fmaxf(t4.z, t4.w)));
+                }
+                mnew[h] = fmaxf(m[h], tmax);
+            }
+            __syncwarp();
+            // each lane exponentiates only the score(s) it owns
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int idx = base + r;
+                const int hidx = idx / C::PPW;
+                float mh = mnew[0];
+#pragma unroll
+                for (int h = 1; h < G; ++h)
+                    if (hidx == h) mh = mnew[h];
+                sc[warp * C::NV + idx] = (own[r] == -INFINITY) ? 0.f : exp2f(own[r] - mh);
             }
             __syncwarp();
             float pr[G][C::PPW];
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-                float s[C::PPW];
+                float psum = 0.f;
 #pragma unroll
                 for (int jj = 0; jj < C::PPW; jj += 4) {
                     const float4 t4 = *reinterpret_cast<const float4 *>(&sc[warp * C::NV + h * C::PPW + jj]);
-                    s[jj] = t4.x; s[jj + 1] = t4.y; s[jj + 2] = t4.z; s[jj + 3] = t4.w;
+                    pr[h][jj] = t4.x; pr[h][jj + 1] = t4.y; pr[h][jj + 2] = t4.z; pr[h][jj + 3] = t4.w;
+                    psum += (t4.x + t4.y) + (t4.z + t4.w);
                 }
-                float tmax = -INFINITY;
+                if (mnew[h] != m[h]) {  // warp-uniform: rescale only when the maximum moved
+                    const float alpha = safe_exp2_diff(m[h], mnew[h]);
+                    l[h] *= alpha;
 #pragma unroll
-                for (int jj = 0; jj < C::PPW; ++jj) {
-                    if (jb + jj >= np) s[jj] = -INFINITY;
-                    tmax = fmaxf(tmax, s[jj]);
+                    for (int v = 0; v < C::VPL; ++v) o[h][v] *= alpha;
+                    m[h] = mnew[h];
                 }
-                const float mnew = fmaxf(m[h], tmax);
-                const float alpha = safe_exp2_diff(m[h], mnew);
-                float psum = 0.f;
-#pragma unroll
-                for (int jj = 0; jj < C::PPW; ++jj) {
-                    pr[h][jj] = (s[jj] == -INFINITY) ? 0.f : exp2f(s[jj] - mnew);
-                    psum += pr[h][jj];
-                }
-                l[h] = l[h] * alpha + psum;
-                m[h] = mnew;
-#pragma unroll
-                for (int v = 0; v < C::VPL; ++v) o[h][v] *= alpha;
+                l[h] += psum;
             }
 #pragma unroll
             for (int jj = 0; jj < C::PPW; ++jj) {

@@ -5,19 +5,17 @@
 // Inputs are bf16 (Q staged by the RoPE kernel, K/V from the cache the same launch sequence
 // appended to), products accumulate in fp32 in tensor memory, softmax runs in fp32.
 //
-// One CTA owns 128 query rows of one (sequence, q-head); warp w owns TMEM lanes 32w..32w+31,
-// i.e. query rows 32w..32w+31 (thread = row).  Per KV tile of 128 positions:
-//   1. TMA (tensor maps, 128-byte swizzle, no multicast) has brought Q once and K_j/V_j into a
-//      two-deep ring; thread 0 issues S = Q K_j^T as 4 tcgen05.mma (M=128, N=128, K=16 each,
-//      A and B K-major from shared memory) into TMEM columns [0,128) and commits to an mbarrier.
-//   2. Every thread loads its row of S (tcgen05.ld), applies the causal mask, updates the
-//      running max / sum (online softmax, log2 domain) and writes P = 2^(s - m) as packed bf16
-//      into TMEM columns [192,256).
-//   3. Thread 0 issues O_j = P V_j as 8 tcgen05.mma with A = P from TMEM and B = V_j from shared
-//      memory (MN-major: V rows are positions, head_dim contiguous) into TMEM columns
-//      [128,192); threads fold O_j into their register accumulator with the rescale factor.
-// KV tiles past the diagonal are skipped.  Every mbarrier wait is bounded (common.cuh); TMEM is
-// released on every exit path.
+// One CTA owns 256 query rows (two tiles of 128) of one (sequence, q-head).  A TMA warp brings
+// Q once and K/V tiles of 128 positions (2-D tensor maps, 128-byte swizzle, no multicast) into a
+// three-deep ring; a single MMA thread issues S_q = Q_q K^T (4 x tcgen05.mma kind::f16, M=128,
+// N=128, K=16, A and B K-major from shared memory) and O_q += P_q V (8 MMAs, A = P from TMEM,
+// B = V MN-major from shared memory); two softmax groups of 128 threads (thread = query row =
+// TMEM lane) load S, mask causally, keep the online max/sum in fp32 (log2 domain), write P as
+// packed bf16 into TMEM and rescale O in TMEM only when a row's maximum grows past 2^8.  S and
+// P have separate TMEM columns, so S_q(j+1) runs on the tensor core while the softmax of
+// S_q(j) is still in flight, and the two query tiles alternate.  KV tiles past the diagonal are
+// skipped.  Every mbarrier wait is bounded (common.cuh); TMEM is released on every exit path
+// after the MMA thread has seen its own last commit.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -34,8 +32,6 @@ constexpr int BM = 128;             // query rows per CTA
 constexpr int BN = 128;             // keys per KV tile
 constexpr int HD = 64;              // head_dim covered by this kernel
 constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB, one 128 x 64 bf16 tile
-constexpr int TMEM_COLS = 256;
-constexpr int COL_S = 0, COL_O = 128, COL_P = 192;
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ---- PTX wrappers ---------------------------------------------------------------------------
@@ -112,6 +108,24 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
         "r"(r[29]), "r"(r[30]), "r"(r[31])                                                          \
         : "memory")
 
+#define TL_LD16(taddr, r)                                                                          \
+    asm volatile(                                                                                  \
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14," \
+        "%15}, [%16];"                                                                             \
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),      \
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),  \
+          "=r"(r[14]), "=r"(r[15])                                                                 \
+        : "r"(taddr))
+
+#define TL_ST16(taddr, r)                                                                          \
+    asm volatile(                                                                                  \
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"  \
+        "%14,%15,%16};" ::"r"(taddr),                                                              \
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),    \
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),           \
+        "r"(r[15])                                                                                  \
+        : "memory")
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -144,180 +158,277 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 struct TcParams {
     HeadView out;
     int nseq, ntok, nHead, nHeadKv;
-    int64_t q_row0;      // staging row of (b=0, h=0, t=0)
     int64_t kv_row_layer;  // cache row of (layer, slot0, kvh=0, pos=0)
     int kv_rows_per_slot;  // nHeadKv * maxLen
     int maxLen;
     unsigned *err;
 };
 
-__global__ void __launch_bounds__(128, 1)
+constexpr int NS_KV = 3;                       // K/V ring depth (32 KB per stage)
+constexpr int THREADS = 384;                   // 3 warpgroups: control, softmax tile 0, softmax tile 1
+constexpr int TMEM_ALL = 512;
+// TMEM columns: S0 | S1 | P0 | P1 | O0 | O1
+__host__ __device__ constexpr int col_s(int q) { return q * 128; }
+__host__ __device__ constexpr int col_p(int q) { return 256 + q * 64; }
+__host__ __device__ constexpr int col_o(int q) { return 384 + q * 64; }
+constexpr float kRescaleThreshold = 8.0f;      // log2 units: O is rescaled only past 2^8
+
+// Each scheduler partition runs one control warp and two softmax warps (warp w sits on
+// partition w % 4).  Registers move from the control warpgroup (104 per thread) to the softmax
+// groups (200): 104 + 2*200 = 504 = 3*168, the allotment of three warps launched at 168.
+__device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 104;"); }
+__device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 200;"); }
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+
+struct Bars {
+    uint64_t q_full, kv_full[NS_KV], kv_empty[NS_KV], s_full[2], s_free[2], p_ready[2], o_bar[2],
+        o_done[2], mma_final;
+    uint32_t tmem_base;
+    int abort;
+};
+
+// Causal prefill, one CTA = 256 query rows (two 128-row tiles) of one (sequence, q-head).
+//   warpgroup 0: warp 0 lane 0 = TMA producer; warp 1 = TMEM owner, its lane 0 the MMA issuer
+//   warpgroups 1 / 2: softmax of query tile 0 / 1, thread = row = TMEM lane (warp w reaches
+//   TMEM lanes 32*(w%4)..)
+// Per KV tile j and query tile q the MMA issuer runs S_q(j+1) = Q_q K_{j+1}^T as soon as the
+// softmax group has pulled S_q(j) into registers (s_free), and O_q += P_q(j) V_j once P_q(j) is
+// in TMEM (p_ready), so the tensor core works on one tile while the other group's softmax runs.
+__global__ void __launch_bounds__(THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
-    // 1024-aligned carve-up: Q | K0 | K1 | V0 | V1 | barriers
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-    uint8_t *sQ = base;
-    uint8_t *sK[2] = {base + TILE_BYTES, base + 2 * TILE_BYTES};
-    uint8_t *sV[2] = {base + 3 * TILE_BYTES, base + 4 * TILE_BYTES};
-    uint64_t *bar = reinterpret_cast<uint64_t *>(base + 5 * TILE_BYTES);
-    uint64_t *bar_q = bar, *bar_kv = bar + 1 /*[2]*/, *bar_mma = bar + 3;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 4);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(bar + 5);
+    uint8_t *sQ[2] = {base, base + TILE_BYTES};
+    uint8_t *sK = base + 2 * TILE_BYTES;                  // [NS_KV] tiles
+    uint8_t *sV = base + (2 + NS_KV) * TILE_BYTES;        // [NS_KV] tiles
+    Bars *bars = reinterpret_cast<Bars *>(base + (2 + 2 * NS_KV) * TILE_BYTES);
+    volatile int *abort_flag = &bars->abort;
 
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int ntiles_q = (p.ntok + BM - 1) / BM;
-    const int qt = ntiles_q - 1 - (int)blockIdx.x;  // heavy (late) tiles first
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int npairs = (p.ntok + 2 * BM - 1) / (2 * BM);
+    const int pair = npairs - 1 - (int)blockIdx.x;  // heavy (late) tiles first
     const int h = blockIdx.y, b = blockIdx.z;
-    const int G = p.nHead / p.nHeadKv;
-    const int g = h / G;
-    const int q0 = qt * BM;
-    const int row = q0 + tid;  // this thread's query position
-    const int nkv = min((q0 + BM + BN - 1) / BN, (p.ntok + BN - 1) / BN);
+    const int g = h / (p.nHead / p.nHeadKv);
+    const int q0 = pair * 2 * BM;
+    int nt[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int start = q0 + q * BM;
+        nt[q] = start < p.ntok ? (min(start + BM, p.ntok) + BN - 1) / BN : 0;
+    }
+    const int nkv = max(nt[0], nt[1]);
 
     if (tid == 0) {
-        mbar_init(bar_q, 1);
-        mbar_init(&bar_kv[0], 1);
-        mbar_init(&bar_kv[1], 1);
-        mbar_init(bar_mma, 1);
-        *abort_flag = 0;
+        mbar_init(&bars->q_full, 1);
+        for (int i = 0; i < NS_KV; ++i) {
+            mbar_init(&bars->kv_full[i], 1);
+            mbar_init(&bars->kv_empty[i], 1);
+        }
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(&bars->s_full[q], 1);
+            mbar_init(&bars->s_free[q], BM);
+            mbar_init(&bars->p_ready[q], BM);
+            mbar_init(&bars->o_bar[q], 1);
+            mbar_init(&bars->o_done[q], 1);
+        }
+        mbar_init(&bars->mma_final, 1);
+        bars->abort = 0;
         fence_mbar_init();
     }
-    if (warp == 0) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == 1) {
+        tmem_alloc(&bars->tmem_base, TMEM_ALL);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    const int qrow = (int)(p.q_row0 + ((int64_t)b * p.nHead + h) * p.ntok + q0);
+    const uint32_t tmem = bars->tmem_base;
+    const int qrow = (int)(((int64_t)b * p.nHead + h) * p.ntok + q0);
     const int kvrow0 = (int)(p.kv_row_layer + (int64_t)b * p.kv_rows_per_slot + (int64_t)g * p.maxLen);
-    if (tid == 0) {
-        mbar_arrive_expect_tx(bar_q, TILE_BYTES);
-        tma_load_2d(sQ, &qmap, 0, qrow, bar_q);
-        mbar_arrive_expect_tx(&bar_kv[0], 2 * TILE_BYTES);
-        tma_load_2d(sK[0], &kmap, 0, kvrow0, &bar_kv[0]);
-        tma_load_2d(sV[0], &vmap, 0, kvrow0, &bar_kv[0]);
-    }
 
-    const float scale = kLog2e / 8.0f;  // log2(e) / sqrt(64)
-    float m = -INFINITY, l = 0.f;
-    float o[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t idesc_s = idesc_bf16(BN, false);
-    const uint32_t idesc_o = idesc_bf16(HD, true);
-    uint32_t mma_phase = 0;
-    bool ok = mbar_wait(bar_q, 0, p.err, abort_flag);
-
-    for (int j = 0; j < nkv && ok; ++j) {
-        const int buf = j & 1;
-        if (!mbar_wait(&bar_kv[buf], (j >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
-        if (tid == 0) {
-            // prefetch the next KV tile into the other buffer (its previous MMAs are complete:
-            // every iteration waits for its own MMAs before the next begins)
-            if (j + 1 < nkv) {
-                const int nb = buf ^ 1;
-                mbar_arrive_expect_tx(&bar_kv[nb], 2 * TILE_BYTES);
-                tma_load_2d(sK[nb], &kmap, 0, kvrow0 + (j + 1) * BN, &bar_kv[nb]);
-                tma_load_2d(sV[nb], &vmap, 0, kvrow0 + (j + 1) * BN, &bar_kv[nb]);
+    if (warp < 4) {
+        setmaxnreg_dec();
+        if (warp == 0 && lane == 0) {
+            // ---------------- TMA producer ----------------
+            mbar_arrive_expect_tx(&bars->q_full, (nt[1] > 0 ? 2 : 1) * TILE_BYTES);
+            tma_load_2d(sQ[0], &qmap, 0, qrow, &bars->q_full);
+            if (nt[1] > 0) tma_load_2d(sQ[1], &qmap, 0, qrow + BM, &bars->q_full);
+            int issued = 0;
+            bool ok = true;
+            for (int j = 0; j < nkv && ok; ++j) {
+                const int st = j % NS_KV;
+                if (!mbar_wait(&bars->kv_empty[st], ((j / NS_KV) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
+                mbar_arrive_expect_tx(&bars->kv_full[st], 2 * TILE_BYTES);
+                tma_load_2d(sK + st * TILE_BYTES, &kmap, 0, kvrow0 + j * BN, &bars->kv_full[st]);
+                tma_load_2d(sV + st * TILE_BYTES, &vmap, 0, kvrow0 + j * BN, &bars->kv_full[st]);
+                ++issued;
             }
+            // wait (bounded) until every copy issued into this CTA's shared memory has landed
+            mbar_wait(&bars->q_full, 0, nullptr, nullptr);
+            for (int j = max(0, issued - NS_KV); j < issued; ++j)
+                mbar_wait(&bars->kv_full[j % NS_KV], (j / NS_KV) & 1, nullptr, nullptr);
+        } else if (warp == 1 && lane == 0) {
+            // ---------------- MMA issuer ----------------
+            const uint32_t idesc_s = idesc_bf16(BN, false);
+            const uint32_t idesc_o = idesc_bf16(HD, true);
+            bool ok = mbar_wait(&bars->q_full, 0, p.err, abort_flag) &&
+                      mbar_wait(&bars->kv_full[0], 0, p.err, abort_flag);
+            auto issue_s = [&](int q, int j) {
+                const uint32_t qa = smem_u32(sQ[q]), ka = smem_u32(sK + (j % NS_KV) * TILE_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk)
+                    mma_ss(tmem + col_s(q), sw128_desc(qa + kk * 32, 16), sw128_desc(ka + kk * 32, 16), idesc_s,
+                           kk > 0 ? 1u : 0u);
+                tc_commit(&bars->s_full[q]);
+            };
+            if (ok) {
+                tc_fence_after();
+                for (int q = 0; q < 2; ++q)
+                    if (nt[q] > 0) issue_s(q, 0);
+            }
+            for (int j = 0; j < nkv && ok; ++j) {
+                for (int q = 0; q < 2 && ok; ++q) {
+                    if (j >= nt[q]) continue;
+                    if (j + 1 < nt[q]) {
+                        ok = mbar_wait(&bars->s_free[q], j & 1, p.err, abort_flag) &&
+                             mbar_wait(&bars->kv_full[(j + 1) % NS_KV], ((j + 1) / NS_KV) & 1, p.err, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_s(q, j + 1);
+                    }
+                    if (!mbar_wait(&bars->p_ready[q], j & 1, p.err, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t va = smem_u32(sV + (j % NS_KV) * TILE_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BN / 16; ++kk)
+                        mma_ts(tmem + col_o(q), tmem + col_p(q) + kk * 8, sw128_desc(va + kk * 2048, TILE_BYTES),
+                               idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&bars->o_bar[q]);
+                    if (j == nt[q] - 1) tc_commit(&bars->o_done[q]);
+                }
+                if (ok) tc_commit(&bars->kv_empty[j % NS_KV]);
+            }
+            // every MMA this thread issued has completed before TMEM can be released
+            tc_commit(&bars->mma_final);
+            mbar_wait(&bars->mma_final, 0, p.err, nullptr);
+        }
+    } else {
+        setmaxnreg_inc();
+        // ---------------- softmax of query tile q ----------------
+        const int q = (warp - 4) >> 2;
+        const int r = (warp & 3) * 32 + lane;
+        const int row = q0 + q * BM + r;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const float C = kLog2e / 8.0f;  // log2(e) / sqrt(64)
+        float m_run = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nt[q] && ok; ++j) {
+            // warp-uniform verdict: the TMEM loads below are warp-collective
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, p.err, abort_flag));
+            if (!ok) break;
             tc_fence_after();
-            const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK[buf]);
+            uint32_t sr[BN];
 #pragma unroll
-            for (int kk = 0; kk < HD / 16; ++kk)
-                mma_ss(tmem + COL_S, sw128_desc(qa + kk * 32, 16), sw128_desc(ka + kk * 32, 16), idesc_s,
-                       kk > 0 ? 1u : 0u);
-            tc_commit(bar_mma);
-        }
-        if (!mbar_wait(bar_mma, mma_phase, p.err, abort_flag)) { ok = false; break; }
-        mma_phase ^= 1u;
-        tc_fence_after();
-
-        // ---- softmax on this thread's row ----
-        uint32_t sr[BN];
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t *rr = sr + 32 * c;
+                TL_LD32(tmem + lane_base + col_s(q) + 32 * c, rr);
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
+            const int k0 = j * BN;
+            if (j == nt[q] - 1) {  // diagonal / ragged tile: causal and length mask
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-            uint32_t *r = sr + 32 * c;
-            TL_LD32(tmem + lane_base + COL_S + 32 * c, r);
-        }
-        tmem_wait_ld();
-        const int k0 = j * BN;
-        const bool diag = (k0 + BN - 1 > row) || (k0 + BN > p.ntok);
-        float mt = -INFINITY;
+                for (int c = 0; c < BN; ++c)
+                    if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
+            }
+            float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-            float s = __uint_as_float(sr[c]) * scale;
-            if (diag && (k0 + c > row || k0 + c >= p.ntok)) s = -INFINITY;
-            sr[c] = __float_as_uint(s);
-            mt = fmaxf(mt, s);
-        }
-        const float mnew = fmaxf(m, mt);
-        const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - mnew);
-        float ps = 0.f;
-        uint32_t pk[BN / 2];
+            for (int c = 0; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+            const float ms = mx * C;
+            const bool grow = ms > m_run + kRescaleThreshold || m_run == -INFINITY;
+            float alpha = 1.f;
+            if (grow) {
+                alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - ms);
+                m_run = ms;
+                l *= alpha;
+            }
+            if (__any_sync(0xffffffffu, grow && j > 0)) {
+                // O_q holds the sum through tile j-1; wait for that PV, then rescale in TMEM
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_bar[q], (j - 1) & 1, p.err, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < BN; c += 2) {
-            const float s0 = __uint_as_float(sr[c]), s1 = __uint_as_float(sr[c + 1]);
-            const float p0 = (s0 == -INFINITY) ? 0.f : exp2f(s0 - mnew);
-            const float p1 = (s1 == -INFINITY) ? 0.f : exp2f(s1 - mnew);
-            ps += p0 + p1;
-            pk[c / 2] = pack_bf16(p0, p1);
-        }
-        l = l * alpha + ps;
-        m = mnew;
+                for (int c = 0; c < HD / 16; ++c) {  // 16 columns at a time: S stays in registers
+                    uint32_t orr[16];
+                    TL_LD16(tmem + lane_base + col_o(q) + 16 * c, orr);
+                    tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            uint32_t *r = pk + 32 * c;
-            TL_ST32(tmem + lane_base + COL_P + 32 * c, r);
+                    for (int i = 0; i < 16; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+                    TL_ST16(tmem + lane_base + col_o(q) + 16 * c, orr);
+                }
+            }
+            const float neg = -m_run;
+            float ps = 0.f;
+            uint32_t pk[BN / 2];
+#pragma unroll
+            for (int c = 0; c < BN; c += 2) {
+                const float p0 = ex2(fmaf(__uint_as_float(sr[c]), C, neg));
+                const float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), C, neg));
+                ps += p0 + p1;
+                pk[c / 2] = pack_bf16(p0, p1);
+            }
+            l += ps;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t *rr = pk + 32 * c;
+                TL_ST32(tmem + lane_base + col_p(q) + 32 * c, rr);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars->p_ready[q]);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
+        if (ok && nt[q] > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], 0, p.err, abort_flag));
+        if (ok && nt[q] > 0) {
             tc_fence_after();
-            const uint32_t va = smem_u32(sV[buf]);
+            uint32_t orr[HD];
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk)
-                mma_ts(tmem + COL_O, tmem + COL_P + kk * 8, sw128_desc(va + kk * 2048, TILE_BYTES), idesc_o,
-                       kk > 0 ? 1u : 0u);
-            tc_commit(bar_mma);
+            for (int c = 0; c < HD / 32; ++c) {
+                uint32_t *rr = orr + 32 * c;
+                TL_LD32(tmem + lane_base + col_o(q) + 32 * c, rr);
+            }
+            tmem_wait_ld();
+            if (row < p.ntok) {
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                float *dst = p.out.ptr;
+#pragma unroll
+                for (int i = 0; i < HD; i += 4) {
+                    const int64_t o = p.out.at(b, row, h, i);
+                    if (p.out.sd == 1 && (o & 3) == 0) {
+                        *reinterpret_cast<float4 *>(dst + o) =
+                            make_float4(__uint_as_float(orr[i]) * inv, __uint_as_float(orr[i + 1]) * inv,
+                                        __uint_as_float(orr[i + 2]) * inv, __uint_as_float(orr[i + 3]) * inv);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) dst[p.out.at(b, row, h, i + u)] = __uint_as_float(orr[i + u]) * inv;
+                    }
+                }
+            }
         }
-        if (!mbar_wait(bar_mma, mma_phase, p.err, abort_flag)) { ok = false; break; }
-        mma_phase ^= 1u;
-        tc_fence_after();
-        uint32_t orr[HD];
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-            uint32_t *r = orr + 32 * c;
-            TL_LD32(tmem + lane_base + COL_O + 32 * c, r);
-        }
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha, __uint_as_float(orr[i]));
-        tc_fence_before();
-        __syncthreads();  // all rows done with S/P/O before the next tile's MMAs overwrite them
-    }
-
-    if (ok && row < p.ntok) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        float *dst = p.out.ptr;
-#pragma unroll
-        for (int i = 0; i < HD; ++i) dst[p.out.at(b, row, h, i)] = o[i] * inv;
-    }
-    // drain outstanding TMA into this CTA's shared memory before it is released
-    if (tid == 0 && !ok) {
-        mbar_wait(&bar_kv[0], 0, nullptr, nullptr);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc(tmem, TMEM_ALL);
     }
 }
 
@@ -357,7 +468,7 @@ cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s) {
         return cudaErrorNotSupported;
     const int64_t q_rows = (int64_t)a.nseq * a.nHead * a.ntok;
     const int64_t kv_rows = (int64_t)a.kv.nLayer * a.kv.maxBatch * a.kv.nHeadKv * a.kv.maxLen;
-    if (q_rows + BM > INT32_MAX || kv_rows + BN > INT32_MAX) return cudaErrorNotSupported;
+    if (q_rows + 2 * BM > INT32_MAX || kv_rows + BN > INT32_MAX) return cudaErrorNotSupported;
     CUtensorMap qm, km, vm;
     if (!make_map(&qm, a.qb, (uint64_t)q_rows) || !make_map(&km, a.kv.k, (uint64_t)kv_rows) ||
         !make_map(&vm, a.kv.v, (uint64_t)kv_rows))
@@ -368,16 +479,15 @@ cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s) {
     p.ntok = a.ntok;
     p.nHead = a.nHead;
     p.nHeadKv = a.nHeadKv;
-    p.q_row0 = 0;
     p.kv_row_layer = a.kv.row(a.layer, a.slot0, 0, 0);
     p.kv_rows_per_slot = a.kv.nHeadKv * a.kv.maxLen;
     p.maxLen = a.kv.maxLen;
     p.err = a.err;
-    const int smem = 5 * TILE_BYTES + 128 + 1024;
+    const int smem = (2 + 2 * NS_KV) * TILE_BYTES + (int)sizeof(Bars) + 1024;
     cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((a.ntok + BM - 1) / BM, a.nHead, a.nseq);
-    prefill_tc_kernel<<<grid, 128, smem, s>>>(qm, km, vm, p);
+    dim3 grid((a.ntok + 2 * BM - 1) / (2 * BM), a.nHead, a.nseq);
+    prefill_tc_kernel<<<grid, THREADS, smem, s>>>(qm, km, vm, p);
     return cudaGetLastError();
 }
 
