@@ -154,7 +154,8 @@ TL_API int tl_decode_attention(tl_attn *h, int layer, int slot0, int nseq, const
                         const int *pos_host, const float *q, float *out, void *stream);
 /* Batched prefill from position 0 (src/forward.nim:271-274 per sequence): q
  * [nseq][seqLen][nHead*headDim], k, v [nseq][seqLen][nHeadKv*headDim], out like q.
- * bf16 cache + headDim 64: tcgen05 tensor-core attention; otherwise fp32 CUDA cores. */
+ * bf16 cache + headDim 64: tcgen05 tensor-core attention, q and k are left unmodified;
+ * otherwise fp32 CUDA cores, q and k are rotated in place. */
 TL_API int tl_prefill_step(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q, float *k,
                     const float *v, float *out, void *stream);
 /* Same as tl_prefill_step but forces the fp32 CUDA-core attention kernel. */

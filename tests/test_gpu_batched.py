@@ -82,7 +82,9 @@ def test_decode_step_batched(env, kvd, Hq, Hkv, D, lens):
             vc[:, L:] = v[b].reshape(-1, 1) if kvd == 0 else bf16_round(v[b].reshape(-1, 1))
             ref = ora.attention_cached(qr, kc, vc, L + 1, Hq, Hkv, D)
             exact = numpy_ref.attention(qr, kc, vc, Hq, Hkv, D, np.array([L]), L + 1) if L >= 1024 else None
-            err, allowed = parity(got[b].reshape(-1, 1), ref, exact, TOL_F32)
+            # bf16 cache: the tensor-core kernel (bf16 hi/lo q and p, fp32 accumulate) is held to
+            # the bf16-KV bound against the oracle fed the same bf16-rounded K/V
+            err, allowed = parity(got[b].reshape(-1, 1), ref, exact, TOL_F32 if kvd == 0 else TOL_BF16)
             assert err <= allowed, (b, L, err, allowed)
         # repeated calls give identical results (counters are reset by the merging CTA)
         out2 = torch.empty_like(out)

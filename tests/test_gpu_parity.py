@@ -129,10 +129,10 @@ def test_attention_cached_matches_oracle(fa, Hq, Hkv, D, L, kvd):
     q = randn(rng, Hq * D, 1)
     ctx = fa.attentionCached(q, cache, 0, L, Hq, Hkv, D)
     ref = ora.attention_cached(q, kc, vc, L, Hq, Hkv, D)
-    # the bf16 cache is compared with the oracle fed the same bf16-rounded K/V, so the fp32
-    # bound applies to both
+    # a bf16 cache is compared with the oracle fed the same bf16-rounded K/V, under the bf16-KV
+    # bound (the tensor-core kernel rounds q and p into bf16 hi/lo parts)
     exact = numpy_ref.attention(q, kc, vc, Hq, Hkv, D, np.array([L - 1]), L) if L >= 1024 else None
-    err, allowed = parity(ctx, ref, exact, TOL_F32)
+    err, allowed = parity(ctx, ref, exact, TOL_F32 if kvd == 0 else TOL_BF16)
     assert err <= allowed, (err, allowed)
 
 
@@ -161,8 +161,11 @@ def test_decode_layer_matches_oracle_step(fa, kvd):
     kc[:, L:L + 1] = kr if kvd == 0 else bf16_round(kr)
     vc[:, L:L + 1] = v if kvd == 0 else bf16_round(v)
     ref = ora.attention_cached(qr, kc, vc, L + 1, 32, 4, 64)
-    assert max_rel_err(ctx, ref) <= TOL_F32
-    assert np.array_equal(cache.k[1][:, L:L + 1], kc[:, L:L + 1])
+    assert max_rel_err(ctx, ref) <= (TOL_F32 if kvd == 0 else TOL_BF16)
+    if kvd == 0:
+        check_rope(cache.k[1][:, L:L + 1], kc[:, L:L + 1])
+    else:
+        assert np.max(np.abs(cache.k[1][:, L:L + 1] - kc[:, L:L + 1])) <= 2 ** -7 * np.max(np.abs(kc[:, L:L + 1]))
 
 
 def test_decode_kv_full(fa):

@@ -20,7 +20,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include")]
 SOURCES = ["tl_attn_api.cu", "rope_append.cu", "decode_attn.cu", "prefill_simt.cu",
-           "prefill_tc.cu", "dist.cu", "decode_noalloc.cu"]
+           "prefill_tc.cu", "dist.cu", "decode_noalloc.cu", "decode_mma.cu"]
 
 
 def _headers() -> list[str]:

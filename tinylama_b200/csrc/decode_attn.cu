@@ -23,13 +23,14 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "decode_common.cuh"
 #include "internal.h"
 
 namespace tl {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kMaxChunksPerSeq = 256;
+
 
 template <typename KV, int D, int G>
 struct DecCfg {
@@ -56,10 +57,6 @@ struct DecCfg {
     static constexpr int OFF_PREFIX = OFF_CW + kMaxChunksPerSeq * G * 4;
     static size_t smem_bytes(int nseq) { return (size_t)OFF_PREFIX + 4 * (size_t)(nseq + 1) + 16; }
 };
-
-__device__ __forceinline__ float safe_exp2_diff(float m, float M) {
-    return (m == -INFINITY) ? 0.f : exp2f(m - M);
-}
 
 // Multi-value butterfly: N partial sums per lane -> after the call, lane holds the full
 // (over 32 lanes) sum of R = max(1, N/32) of the N values in v[0..R).  The original index of
@@ -98,49 +95,6 @@ __device__ __forceinline__ int butterfly_index(int lane) {
     return idx;
 }
 
-__device__ __forceinline__ size_t decode_partial_floats_dev(int total_units, int group, int d) {
-    return (size_t)total_units * group * (d + 2);
-}
-
-struct Unit {
-    int b, g, c, nch, n, p0, p1;
-};
-
-__device__ __forceinline__ int local_len(const DecodeArgs &a, int b, unsigned *err) {
-    const int pos = a.pos[b];
-    const int slice = a.kv.maxLen;
-    if (pos < 0 || pos - a.pos_offset >= slice) {
-        // single-GPU: the appended token must sit inside the cache
-        if (a.lse_out == nullptr || pos < 0) atomicOr(err, TL_DEVERR_POS_RANGE);
-    }
-    int n = pos + 1 - a.pos_offset;
-    n = n < 0 ? 0 : (n > slice ? slice : n);
-    return n;
-}
-
-__device__ __forceinline__ int nchunks(int n, int C) { return n <= 0 ? 1 : (n + C - 1) / C; }
-
-__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, const int *prefix, const int *lens,
-                                            int u) {
-    Unit r;
-    r.g = u % a.nHeadKv;
-    const int t = u / a.nHeadKv;
-    // upper_bound over prefix[0..nseq] for t
-    int lo = 0, hi = a.nseq;  // prefix[lo] <= t < prefix[hi]
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (prefix[mid] <= t) lo = mid; else hi = mid;
-    }
-    r.b = lo;
-    r.c = t - prefix[lo];
-    r.nch = prefix[lo + 1] - prefix[lo];
-    r.n = lens[lo];
-    r.p0 = r.c * a.chunk;
-    r.p1 = min(r.p0 + a.chunk, r.n);
-    if (r.p1 < r.p0) r.p1 = r.p0;
-    return r;
-}
-
 template <typename KV, int D, int G>
 __global__ void __launch_bounds__(DecCfg<KV, D, G>::THREADS)
 decode_kernel(const DecodeArgs a) {
@@ -172,32 +126,7 @@ decode_kernel(const DecodeArgs a) {
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 0) {
-        const int per = (a.nseq + 31) / 32;
-        const int s0 = lane * per, s1 = min(s0 + per, a.nseq);
-        int sum = 0, mx = 0;
-        for (int s = s0; s < s1; ++s) {
-            const int n = local_len(a, s, err);
-            lens[s] = n;
-            sum += nchunks(n, a.chunk);
-            mx = max(mx, nchunks(n, a.chunk));
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) max_nch[0] = mx;
-        int incl = sum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-        }
-        int run = incl - sum;
-        for (int s = s0; s < s1; ++s) {
-            prefix[s] = run;
-            run += nchunks(lens[s], a.chunk);
-        }
-        if (lane == 31) prefix[a.nseq] = incl;
-    }
+    if (warp == 0) build_schedule(a, prefix, lens, max_nch, lane, err);
     __syncthreads();
     const int total_units = prefix[a.nseq] * a.nHeadKv;
     // The host sizes the scratch and the chunk length; refuse (uniformly) if they do not fit.
@@ -371,86 +300,7 @@ decode_kernel(const DecodeArgs a) {
 #pragma unroll
             for (int v = 0; v < C::VPL; ++v) wo[(warp * G + h) * D + lane * C::VPL + v] = o[h][v];
         }
-        named_bar(1, C::NW * 32);
-        const bool single = (un.nch == 1) && (a.lse_out == nullptr);
-        const int unit_index = u;  // partial slot of this unit
-        for (int e = tid; e < G * D; e += C::NW * 32) {
-            const int h = e / D, dd = e - h * D;
-            float M = -INFINITY;
-#pragma unroll
-            for (int w = 0; w < C::NW; ++w) M = fmaxf(M, wm[w * G + h]);
-            float L = 0.f, O = 0.f;
-#pragma unroll
-            for (int w = 0; w < C::NW; ++w) {
-                const float sw = safe_exp2_diff(wm[w * G + h], M);
-                L = fmaf(wl[w * G + h], sw, L);
-                O = fmaf(wo[(w * G + h) * D + dd], sw, O);
-            }
-            const int head = un.g * G + h;
-            if (single) {
-                a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
-            } else if (un.nch == 1) {
-                float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);
-                dst[dd] = O;
-                if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
-            } else {
-                float *dst = a.partial + ((int64_t)unit_index * G + h) * (D + 2);
-                dst[dd] = O;
-                if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
-            }
-        }
-        if (un.nch > 1) {
-            __threadfence();
-            named_bar(1, C::NW * 32);
-            if (tid == 0) {
-                const unsigned old = atomicAdd(&a.counter[un.b * a.nHeadKv + un.g], 1u);
-                *is_last_flag = (old == (unsigned)(un.nch - 1)) ? 1 : 0;
-            }
-            named_bar(1, C::NW * 32);
-            if (*is_last_flag) {
-                __threadfence();
-                // per-head max / sum over the chunks (warp h handles heads h, h+4, ...)
-                for (int h = warp; h < G; h += C::NW) {
-                    float M = -INFINITY;
-                    for (int c = lane; c < un.nch; c += 32) {
-                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
-                        M = fmaxf(M, __ldcg(&a.partial[((int64_t)uc * G + h) * (D + 2) + D]));
-                    }
-#pragma unroll
-                    for (int o2 = 16; o2 >= 1; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-                    float L = 0.f;
-                    for (int c = lane; c < un.nch; c += 32) {
-                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
-                        const float *pp = &a.partial[((int64_t)uc * G + h) * (D + 2) + D];
-                        const float w = safe_exp2_diff(__ldcg(pp), M);
-                        cw[c * G + h] = w;
-                        L = fmaf(__ldcg(pp + 1), w, L);
-                    }
-#pragma unroll
-                    for (int o2 = 16; o2 >= 1; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
-                    if (lane == 0) { wm[h] = M; wl[h] = L; }
-                }
-                named_bar(1, C::NW * 32);
-                for (int e = tid; e < G * D; e += C::NW * 32) {
-                    const int h = e / D, dd = e - h * D;
-                    float O = 0.f;
-                    for (int c = 0; c < un.nch; ++c) {
-                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
-                        O = fmaf(cw[c * G + h], __ldcg(&a.partial[((int64_t)uc * G + h) * (D + 2) + dd]), O);
-                    }
-                    const int head = un.g * G + h;
-                    const float L = wl[h];
-                    if (a.lse_out == nullptr) {
-                        a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
-                    } else {
-                        float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);
-                        dst[dd] = O;
-                        if (dd == 0) { dst[D] = wm[h]; dst[D + 1] = L; }
-                    }
-                }
-                if (tid == 0) a.counter[un.b * a.nHeadKv + un.g] = 0u;
-            }
-        }
+        unit_epilogue<G, D, C::NW>(a, un, u, prefix, wm, wl, wo, cw, is_last_flag, tid, warp, lane);
         // shared scratch is reused by the next unit; leave together if any warp aborted
         if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
     }
@@ -514,6 +364,12 @@ int occ_t() {
 }  // namespace
 
 cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
+    if (decode_mma_covers(a.headDim, a.nHead / a.nHeadKv, a.kv.dtype)) {
+        // bf16 cache: tensor-core kernel; the CUDA-core kernel below is used only if its tensor
+        // maps cannot be built
+        const cudaError_t e = launch_decode_mma(a, num_ctas, s);
+        if (e != cudaErrorNotSupported) return e;
+    }
     if (a.headDim == 64) {
         return a.kv.dtype == TL_KV_F32 ? launch_g<float, 64>(a, num_ctas, s)
                                        : launch_g<__nv_bfloat16, 64>(a, num_ctas, s);
@@ -528,6 +384,17 @@ cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
 static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype);
 
 int decode_ctas_per_sm(int headDim, int group, int dtype) {
+    if (decode_mma_covers(headDim, group, dtype)) {
+        static int mcache[16][2][9];
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 0 && dev < 16 && group >= 1 && group <= 8) {
+            int &slot = mcache[dev][headDim == 128][group];
+            if (slot == 0) slot = decode_mma_ctas_per_sm(headDim, group);
+            return slot;
+        }
+        return decode_mma_ctas_per_sm(headDim, group);
+    }
     // occupancy of each kernel instance, queried once per process and device
     static int cache[16][2][2][9];  // [device][headDim 64/128][dtype][group]
     int dev = 0;

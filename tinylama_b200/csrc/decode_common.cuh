@@ -1,0 +1,198 @@
+// decode_common.cuh -- work schedule and chunk merge shared by the decode kernels
+// (decode_attn.cu: CUDA-core kernel; decode_mma.cu: tensor-core kernel for bf16 caches).
+//
+// A launch covers (sequence, kv-head, chunk of `chunk` positions) work units.  Each CTA builds
+// the schedule itself (a warp scan over the sequences' lengths), walks units with a grid
+// stride, and at the end of a unit merges its consumer warps' online-softmax states.  A unit
+// that covers a whole sequence writes ctx; otherwise it writes its (o, m, l) partial and the
+// last CTA to finish a (sequence, kv-head) merges all chunks of it (threadfence + arrival
+// counter; nothing waits on anything).
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace tl {
+
+constexpr int kMaxChunksPerSeq = 256;
+
+__device__ __forceinline__ float safe_exp2_diff(float m, float M) {
+    return (m == -INFINITY) ? 0.f : exp2f(m - M);
+}
+
+__device__ __forceinline__ size_t decode_partial_floats_dev(int total_units, int group, int d) {
+    return (size_t)total_units * group * (d + 2);
+}
+
+struct Unit {
+    int b, g, c, nch, n, p0, p1;
+};
+
+__device__ __forceinline__ int local_len(const DecodeArgs &a, int b, unsigned *err) {
+    const int pos = a.pos[b];
+    const int slice = a.kv.maxLen;
+    if (pos < 0 || pos - a.pos_offset >= slice) {
+        // single-GPU: the appended token must sit inside the cache
+        if (a.lse_out == nullptr || pos < 0) atomicOr(err, TL_DEVERR_POS_RANGE);
+    }
+    int n = pos + 1 - a.pos_offset;
+    n = n < 0 ? 0 : (n > slice ? slice : n);
+    return n;
+}
+
+__device__ __forceinline__ int nchunks(int n, int C) { return n <= 0 ? 1 : (n + C - 1) / C; }
+
+__device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, const int *prefix, const int *lens,
+                                            int u) {
+    Unit r;
+    r.g = u % a.nHeadKv;
+    const int t = u / a.nHeadKv;
+    // upper_bound over prefix[0..nseq] for t
+    int lo = 0, hi = a.nseq;  // prefix[lo] <= t < prefix[hi]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (prefix[mid] <= t) lo = mid; else hi = mid;
+    }
+    r.b = lo;
+    r.c = t - prefix[lo];
+    r.nch = prefix[lo + 1] - prefix[lo];
+    r.n = lens[lo];
+    r.p0 = r.c * a.chunk;
+    r.p1 = min(r.p0 + a.chunk, r.n);
+    if (r.p1 < r.p0) r.p1 = r.p0;
+    return r;
+}
+
+// Warp 0: per-sequence local lengths, chunk counts and their exclusive prefix.
+__device__ __forceinline__ void build_schedule(const DecodeArgs &a, int *prefix, int *lens, int *max_nch,
+                                               int lane, unsigned *err) {
+        const int per = (a.nseq + 31) / 32;
+        const int s0 = lane * per, s1 = min(s0 + per, a.nseq);
+        int sum = 0, mx = 0;
+        for (int s = s0; s < s1; ++s) {
+            const int n = local_len(a, s, err);
+            lens[s] = n;
+            sum += nchunks(n, a.chunk);
+            mx = max(mx, nchunks(n, a.chunk));
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) max_nch[0] = mx;
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int run = incl - sum;
+        for (int s = s0; s < s1; ++s) {
+            prefix[s] = run;
+            run += nchunks(lens[s], a.chunk);
+        }
+        if (lane == 31) prefix[a.nseq] = incl;
+    }
+
+// Merge of the NW consumer warps' states (written to wm[NW][G], wl[NW][G], wo[NW][G][D]) at the
+// end of unit u, then the cross-chunk merge by the last CTA.  Called by the NW*32 consumer
+// threads of the CTA; uses named barrier 1.
+template <int G, int D, int NW>
+__device__ __forceinline__ void unit_epilogue(const DecodeArgs &a, const Unit &un, int u, const int *prefix,
+                                              float *wm, float *wl, float *wo, float *cw, int *is_last_flag,
+                                              int tid, int warp, int lane) {
+        named_bar(1, NW * 32);
+        const bool single = (un.nch == 1) && (a.lse_out == nullptr);
+        const int unit_index = u;  // partial slot of this unit
+        for (int e = tid; e < G * D; e += NW * 32) {
+            const int h = e / D, dd = e - h * D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * G + h]);
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float sw = safe_exp2_diff(wm[w * G + h], M);
+                L = fmaf(wl[w * G + h], sw, L);
+                O = fmaf(wo[(w * G + h) * D + dd], sw, O);
+            }
+            const int head = un.g * G + h;
+            if (single) {
+                a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
+            } else if (un.nch == 1) {
+                float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);
+                dst[dd] = O;
+                if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
+            } else {
+                float *dst = a.partial + ((int64_t)unit_index * G + h) * (D + 2);
+                dst[dd] = O;
+                if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
+            }
+        }
+        if (un.nch > 1) {
+            __threadfence();
+            named_bar(1, NW * 32);
+            if (tid == 0) {
+                const unsigned old = atomicAdd(&a.counter[un.b * a.nHeadKv + un.g], 1u);
+                *is_last_flag = (old == (unsigned)(un.nch - 1)) ? 1 : 0;
+            }
+            named_bar(1, NW * 32);
+            if (*is_last_flag) {
+                __threadfence();
+                // per-head max / sum over the chunks (warp h handles heads h, h+4, ...)
+                for (int h = warp; h < G; h += NW) {
+                    float M = -INFINITY;
+                    for (int c = lane; c < un.nch; c += 32) {
+                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
+                        M = fmaxf(M, __ldcg(&a.partial[((int64_t)uc * G + h) * (D + 2) + D]));
+                    }
+#pragma unroll
+                    for (int o2 = 16; o2 >= 1; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+                    float L = 0.f;
+                    for (int c = lane; c < un.nch; c += 32) {
+                        const int uc = (prefix[un.b] + c) * a.nHeadKv + un.g;
+                        const float *pp = &a.partial[((int64_t)uc * G + h) * (D + 2) + D];
+                        const float w = safe_exp2_diff(__ldcg(pp), M);
+                        cw[c * G + h] = w;
+                        L = fmaf(__ldcg(pp + 1), w, L);
+                    }
+#pragma unroll
+                    for (int o2 = 16; o2 >= 1; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+                    if (lane == 0) { wm[h] = M; wl[h] = L; }
+                }
+                named_bar(1, NW * 32);
+                for (int e = tid; e < G * D; e += NW * 32) {
+                    const int h = e / D, dd = e - h * D;
+                    float O = 0.f;
+                    // partials of consecutive chunks are a fixed stride apart; four independent
+                    // accumulators keep several L2 loads in flight
+                    const int64_t stride = (int64_t)a.nHeadKv * G * (D + 2);
+                    const float *src = a.partial + ((int64_t)(prefix[un.b] * a.nHeadKv + un.g) * G + h) * (D + 2) + dd;
+                    float O1 = 0.f, O2 = 0.f, O3 = 0.f;
+                    int c = 0;
+                    for (; c + 4 <= un.nch; c += 4) {
+                        const float x0 = __ldcg(src + (c + 0) * stride), x1 = __ldcg(src + (c + 1) * stride);
+                        const float x2 = __ldcg(src + (c + 2) * stride), x3 = __ldcg(src + (c + 3) * stride);
+                        O = fmaf(cw[(c + 0) * G + h], x0, O);
+                        O1 = fmaf(cw[(c + 1) * G + h], x1, O1);
+                        O2 = fmaf(cw[(c + 2) * G + h], x2, O2);
+                        O3 = fmaf(cw[(c + 3) * G + h], x3, O3);
+                    }
+                    for (; c < un.nch; ++c) O = fmaf(cw[c * G + h], __ldcg(src + c * stride), O);
+                    O = (O + O1) + (O2 + O3);
+                    const int head = un.g * G + h;
+                    const float L = wl[h];
+                    if (a.lse_out == nullptr) {
+                        a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
+                    } else {
+                        float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);
+                        dst[dd] = O;
+                        if (dd == 0) { dst[D] = wm[h]; dst[D + 1] = L; }
+                    }
+                }
+                if (tid == 0) a.counter[un.b * a.nHeadKv + un.g] = 0u;
+            }
+        }
+}
+
+}  // namespace tl

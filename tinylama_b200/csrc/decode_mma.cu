@@ -1,0 +1,395 @@
+// decode_mma.cu -- split-KV decode attention for bf16 KV caches on the tensor cores.
+//
+// Same contract and schedule as the CUDA-core kernel in decode_attn.cu (attentionCached,
+// src/forward.nim:179-211, batched), for caches stored in bf16.  With grouped-query attention
+// the G q-heads of a kv-head share every K/V row, so per row the work is a tiny matrix product:
+// S[G x T] = Q[G x d] K^T[d x T] and O[G x d] += P[G x T] V[T x d].  On the CUDA cores that costs
+// ~G*d/16 FMAs plus cross-lane reductions per row; here it is a few warp-level
+// mma.sync.m16n8k16 (bf16 in, fp32 accumulate) per 8 rows, with the G heads as the M rows of
+// the fragment, so the kernel stays at the HBM roofline for any G <= 8.
+//
+//  * warp 4 (producer): 2-D TMA (tensor map over the whole cache, 64-column boxes with the
+//    128-byte swizzle, no multicast) brings K and V tiles of T = 64 positions into an
+//    NS-stage ring guarded by full/empty mbarriers.
+//  * warps 0..3 (consumers): warp w owns positions 16w..16w+15 of every tile.
+//      S = Q K^T: A = q with its bf16 hi part in fragment rows 0..7 and lo part in rows 8..15
+//        (q keeps ~16 mantissa bits at the cost of one instruction), B = K fragments from
+//        ldmatrix on the swizzled tile;
+//      online softmax on the C fragment (row = head, reductions over the 4 lanes of a quad,
+//        log2 domain, rescale only when the maximum grows past 2^8);
+//      O += P V: the C fragment of S becomes the A fragment of P (hi rows 0..7, lo rows 8..15),
+//        B = V fragments from ldmatrix.trans.
+//  * end of unit: the warps' states go through shared memory to the shared merge
+//    (decode_common.cuh).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "decode_common.cuh"
+#include "internal.h"
+
+namespace tl {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.0f;
+
+template <int D, int G>
+struct MmaCfg {
+    static constexpr int T = 64;                     // positions per tile
+    static constexpr int NW = 4;                     // consumer warps, 16 positions each
+    static constexpr int THREADS = 32 * (NW + 1);
+    static constexpr int HALVES = D / 64;            // 64-column boxes per row
+    static constexpr int HALF_BYTES = T * 128;       // one box: 64 rows x 128 B
+    static constexpr int TILE_BYTES = HALVES * HALF_BYTES;
+    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+    static constexpr int NS = D == 128 ? 3 : 4;
+    static constexpr int KT = D / 16;                // k16 steps over head_dim
+    static constexpr int NT = D / 8;                 // n8 tiles over head_dim
+    static constexpr int OFF_STAGES = 0;             // 1024-aligned (swizzle atoms)
+    static constexpr int OFF_BARS = NS * STAGE_BYTES;
+    static constexpr int OFF_WM = OFF_BARS + 2 * NS * 8 + 16;
+    static constexpr int OFF_WL = OFF_WM + NW * G * 4;
+    static constexpr int OFF_WO = OFF_WL + NW * G * 4;
+    static constexpr int OFF_CW = OFF_WO + NW * G * D * 4;
+    static constexpr int OFF_PREFIX = OFF_CW + kMaxChunksPerSeq * G * 4;
+    static size_t smem_bytes(int nseq) { return 1024 + (size_t)OFF_PREFIX + 4 * (2 * (size_t)nseq + 1) + 16; }
+};
+
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// D += A * B, m16n8k16, bf16 inputs, fp32 accumulators.  With G <= 8 heads, A rows 0..7 carry
+// the bf16 "hi" part of q (or p) and rows 8..15 the "lo" remainder, so one instruction yields
+// both products: d0,d1 = hi . B (row gid) and d2,d3 = lo . B (row gid+8), summed by the lane.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+// bf16 hi/lo split of a pair: x = hi + lo with |lo| <= 2^-9 |x|, both bf16
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = pack2(x0 - __low2float(h), x1 - __high2float(h));
+}
+
+// address of 16-byte chunk `chunk` (0..7) of row `row` in a swizzled 64-column box
+__device__ __forceinline__ uint32_t swz(uint32_t box, int row, int chunk) {
+    return box + row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(MmaCfg<D, G>::THREADS)
+decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                  const DecodeArgs a) {
+    using C = MmaCfg<D, G>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::OFF_BARS);
+    uint64_t *empty = full + C::NS;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + C::NS);
+    int *is_last_flag = const_cast<int *>(reinterpret_cast<volatile int *>(abort_flag) + 1);
+    int *max_nch = is_last_flag + 1;
+    float *wm = reinterpret_cast<float *>(smem + C::OFF_WM);
+    float *wl = reinterpret_cast<float *>(smem + C::OFF_WL);
+    float *wo = reinterpret_cast<float *>(smem + C::OFF_WO);
+    float *cw = reinterpret_cast<float *>(smem + C::OFF_CW);
+    int *prefix = reinterpret_cast<int *>(smem + C::OFF_PREFIX);
+    int *lens = prefix + (a.nseq + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    unsigned *err = a.err;
+    if (tid == 0) {
+        for (int s = 0; s < C::NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], C::NW);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) build_schedule(a, prefix, lens, max_nch, lane, err);
+    __syncthreads();
+    const int total_units = prefix[a.nseq] * a.nHeadKv;
+    if (max_nch[0] > kMaxChunksPerSeq ||
+        (max_nch[0] > 1 && decode_partial_floats_dev(total_units, G, D) > a.partial_cap)) {
+        if (tid == 0) atomicOr(err, TL_DEVERR_BAD_ARG);
+        return;
+    }
+
+    if (warp == C::NW) {
+        // ================= producer =================
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int stage = 0;
+            uint32_t phase = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+                const Unit un = decode_unit(a, prefix, lens, u);
+                const int row0 = (int)a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
+                for (int p = un.p0; p < un.p1; p += C::T) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, abort_flag)) { ok = false; break; }
+                    uint8_t *st = smem + C::OFF_STAGES + stage * C::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+#pragma unroll
+                    for (int hh = 0; hh < C::HALVES; ++hh) {
+                        tma_load_2d(st + hh * C::HALF_BYTES, &kmap, 64 * hh, row0 + p, &full[stage], pol);
+                        tma_load_2d(st + C::TILE_BYTES + hh * C::HALF_BYTES, &vmap, 64 * hh, row0 + p, &full[stage], pol);
+                    }
+                    ++issued;
+                    if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // wait (bounded) for every copy issued into this CTA's shared memory
+            const int outstanding = issued < (long)C::NS ? (int)issued : C::NS;
+            int s = stage;
+            uint32_t ph = phase;
+            for (int i = 0; i < outstanding; ++i) {
+                if (--s < 0) { s = C::NS - 1; ph ^= 1u; }
+                mbar_wait(&full[s], ph, err, nullptr);
+            }
+        }
+        return;
+    }
+
+    // ================= consumers =================
+    const int gid = lane >> 2, tq = lane & 3;  // fragment row (head) and column pair
+    const bool row_ok = gid < G;
+    const float C2 = kLog2e / sqrtf((float)D);
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+        const Unit un = decode_unit(a, prefix, lens, u);
+        // q fragments (A rows = heads of this kv group; rows >= G are zero), bf16 hi + lo
+        uint32_t qh[C::KT][2], ql[C::KT][2];
+        {
+            const float *qrow = a.q + ((int64_t)un.b * a.nHead + (int64_t)un.g * G + (row_ok ? gid : 0)) * D;
+#pragma unroll
+            for (int kt = 0; kt < C::KT; ++kt) {
+                float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+                if (row_ok) {
+                    const float2 lo = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq);
+                    const float2 hi = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq + 8);
+                    x0 = lo.x; x1 = lo.y; x2 = hi.x; x3 = hi.y;
+                }
+                split2(x0, x1, qh[kt][0], ql[kt][0]);
+                split2(x2, x3, qh[kt][1], ql[kt][1]);
+            }
+        }
+        float m = -INFINITY, l = 0.f;
+        float o[C::NT][4];
+#pragma unroll
+        for (int nt = 0; nt < C::NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+        bool ok = true;
+        for (int p = un.p0; p < un.p1; p += C::T) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, err, abort_flag));
+            if (!ok) break;
+            const uint32_t kbox = smem_u32(smem + C::OFF_STAGES + stage * C::STAGE_BYTES);
+            const uint32_t vbox = kbox + C::TILE_BYTES;
+            const int r0 = warp * 16;  // first tile row of this warp
+            // ---- S = Q K^T for 16 positions: two n8 tiles ----
+            float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            {
+                const int krow = r0 + ((lane >> 4) << 3) + (lane & 7);  // n tile = lane >> 4
+                const int kc = (lane >> 3) & 1;                          // 8-dim half of the k16 step
+#pragma unroll
+                for (int kt = 0; kt < C::KT; ++kt) {
+                    const int dim = 16 * kt + 8 * kc;
+                    uint32_t b00, b01, b10, b11;
+                    ldsm_x4(swz(kbox + (dim >> 6) * C::HALF_BYTES, krow, (dim & 63) >> 3), b00, b01, b10, b11);
+                    mma16816(s[0], qh[kt][0], ql[kt][0], qh[kt][1], ql[kt][1], b00, b01);
+                    mma16816(s[1], qh[kt][0], ql[kt][0], qh[kt][1], ql[kt][1], b10, b11);
+                }
+            }
+            // ---- online softmax on row gid (positions 2tq, 2tq+1 of each n8 tile) ----
+            const int pbase = p + r0 + 2 * tq;
+            // score = hi row + lo row of the fragment
+            float v[4] = {(s[0][0] + s[0][2]) * C2, (s[0][1] + s[0][3]) * C2, (s[1][0] + s[1][2]) * C2,
+                          (s[1][1] + s[1][3]) * C2};
+            const int pos[4] = {pbase, pbase + 1, pbase + 8, pbase + 9};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (pos[i] >= un.p1) v[i] = -INFINITY;
+            float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            if (mx > m + kRescale || (m == -INFINITY && mx != -INFINITY)) {
+                // quad-uniform: the four lanes of a row share mx and m
+                const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - mx);
+                m = mx;
+                l *= alpha;
+#pragma unroll
+                for (int nt = 0; nt < C::NT; ++nt) {
+                    o[nt][0] *= alpha;
+                    o[nt][1] *= alpha;
+                    o[nt][2] *= alpha;
+                    o[nt][3] *= alpha;
+                }
+            }
+            float pr[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pr[i] = (v[i] == -INFINITY) ? 0.f : exp2f(v[i] - m);
+            float ps = (pr[0] + pr[1]) + (pr[2] + pr[3]);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            l += ps;
+            // ---- O += P V: P as the A fragment (k = the 16 positions), hi + lo ----
+            uint32_t ph0, pl0, ph1, pl1;
+            split2(pr[0], pr[1], ph0, pl0);  // row gid, k = 2tq, 2tq+1
+            split2(pr[2], pr[3], ph1, pl1);  // row gid, k = 2tq+8, 2tq+9
+            {
+                const int vrow = r0 + (((lane >> 3) & 1) << 3) + (lane & 7);
+                const int vc = lane >> 4;  // which n8 tile of the pair
+#pragma unroll
+                for (int dp = 0; dp < C::NT / 2; ++dp) {
+                    const int dim = 16 * dp + 8 * vc;
+                    uint32_t b00, b01, b10, b11;
+                    ldsm_x4_t(swz(vbox + (dim >> 6) * C::HALF_BYTES, vrow, (dim & 63) >> 3), b00, b01, b10, b11);
+                    mma16816(o[2 * dp], ph0, pl0, ph1, pl1, b00, b01);
+                    mma16816(o[2 * dp + 1], ph0, pl0, ph1, pl1, b10, b11);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+        }
+        // ---- hand this warp's state to the merge (rows gid < G) ----
+        if (row_ok) {
+            if (tq == 0) {
+                wm[warp * G + gid] = m;
+                wl[warp * G + gid] = l;
+            }
+#pragma unroll
+            for (int nt = 0; nt < C::NT; ++nt) {
+                float *dst = wo + (warp * G + gid) * D + 8 * nt + 2 * tq;
+                dst[0] = o[nt][0] + o[nt][2];  // hi rows + lo rows
+                dst[1] = o[nt][1] + o[nt][3];
+            }
+        }
+        unit_epilogue<G, D, C::NW>(a, un, u, prefix, wm, wl, wo, cw, is_last_flag, tid, warp, lane);
+        if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D map over a whole bf16 cache: rows = layer*slot*kvHead*pos, D columns; box 64 x 64.
+bool make_cache_map(CUtensorMap *m, const void *ptr, uint64_t rows, int D) {
+    auto enc = get_encode();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    cuuint32_t box[2] = {64, 64};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D, int G>
+cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
+    using C = MmaCfg<D, G>;
+    const uint64_t rows = (uint64_t)a.kv.nLayer * a.kv.maxBatch * a.kv.nHeadKv * a.kv.maxLen;
+    if (rows + C::T > (uint64_t)INT32_MAX) return cudaErrorNotSupported;
+    CUtensorMap km, vm;
+    if (!make_cache_map(&km, a.kv.k, rows, D) || !make_cache_map(&vm, a.kv.v, rows, D)) return cudaErrorNotSupported;
+    const size_t smem = C::smem_bytes(a.nseq);
+    auto kern = decode_mma_kernel<D, G>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<num_ctas, C::THREADS, smem, s>>>(km, vm, a);
+    return cudaGetLastError();
+}
+
+template <int D, int G>
+int occ_t() {
+    using C = MmaCfg<D, G>;
+    int n = 0;
+    const size_t smem = C::smem_bytes(256);
+    cudaFuncSetAttribute(decode_mma_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<D, G>, C::THREADS, smem) != cudaSuccess)
+        n = 1;
+    return n < 1 ? 1 : n;
+}
+
+}  // namespace
+
+bool decode_mma_covers(int headDim, int group, int dtype) {
+    return dtype == TL_KV_BF16 && (headDim == 64 || headDim == 128) &&
+           (group == 1 || group == 2 || group == 4 || group == 8);
+}
+
+cudaError_t launch_decode_mma(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
+    const int G = a.nHead / a.nHeadKv;
+#define TL_MMA_CASE(DD)                                           \
+    switch (G) {                                                  \
+        case 1: return launch_t<DD, 1>(a, num_ctas, s);           \
+        case 2: return launch_t<DD, 2>(a, num_ctas, s);           \
+        case 4: return launch_t<DD, 4>(a, num_ctas, s);           \
+        case 8: return launch_t<DD, 8>(a, num_ctas, s);           \
+        default: return cudaErrorNotSupported;                    \
+    }
+    if (a.kv.dtype != TL_KV_BF16) return cudaErrorNotSupported;
+    if (a.headDim == 64) { TL_MMA_CASE(64) }
+    if (a.headDim == 128) { TL_MMA_CASE(128) }
+#undef TL_MMA_CASE
+    return cudaErrorNotSupported;
+}
+
+int decode_mma_ctas_per_sm(int headDim, int group) {
+#define TL_MMA_OCC(DD)                         \
+    switch (group) {                           \
+        case 1: return occ_t<DD, 1>();         \
+        case 2: return occ_t<DD, 2>();         \
+        case 4: return occ_t<DD, 4>();         \
+        case 8: return occ_t<DD, 8>();         \
+        default: return 1;                     \
+    }
+    if (headDim == 64) { TL_MMA_OCC(64) }
+    if (headDim == 128) { TL_MMA_OCC(128) }
+#undef TL_MMA_OCC
+    return 1;
+}
+
+}  // namespace tl

@@ -94,6 +94,7 @@ struct RopeAppendArgs {
     const int *pos0;
     int pos0_scalar;
     bool rope_q, rope_k, store;
+    bool q_inplace = true, k_inplace = true;  // write rotated q / k back into their views
     int layer, slot0;  // cache layer and first slot (sequence b -> slot slot0 + b)
     KvLayout kv;
     void *qb;          // nullable: bf16 copy of rotated q, [nseq][nHead][ntok][headDim]
@@ -123,6 +124,10 @@ struct DecodeArgs {
 };
 cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s);
 int decode_ctas_per_sm(int headDim, int group, int dtype);
+// tensor-core decode for bf16 caches (decode_mma.cu)
+bool decode_mma_covers(int headDim, int group, int dtype);
+cudaError_t launch_decode_mma(const DecodeArgs &a, int num_ctas, cudaStream_t s);
+int decode_mma_ctas_per_sm(int headDim, int group);
 size_t decode_partial_floats(int total_units, int group, int headDim);
 
 // Merge G per-rank (o, m, l) partials [G][nseq][nHead][d+2] into out [nseq][nHead][d].

@@ -179,6 +179,29 @@ constexpr float kRescaleThreshold = 8.0f;      // log2 units: O is rescaled only
 __device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 104;"); }
 __device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 200;"); }
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// packed fp32 pair arithmetic (one instruction for two lanes of work)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long *>(&a)), "l"(*reinterpret_cast<unsigned long long *>(&b)),
+          "l"(*reinterpret_cast<unsigned long long *>(&c)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long *>(&a)), "l"(*reinterpret_cast<unsigned long long *>(&b)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -350,9 +373,15 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 for (int c = 0; c < BN; ++c)
                     if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
             }
-            float mx = -INFINITY;
+            // row maximum: four independent chains of three-input max
+            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+            for (int c = 0; c < BN; c += 8) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    mq[u] = max3f(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+            }
+            const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
             const float ms = mx * C;
             const bool grow = ms > m_run + kRescaleThreshold || m_run == -INFINITY;
             float alpha = 1.f;
@@ -376,17 +405,21 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                     TL_ST16(tmem + lane_base + col_o(q) + 16 * c, orr);
                 }
             }
-            const float neg = -m_run;
-            float ps = 0.f;
+            // p = 2^(s*C - m): the argument in packed pairs, the sum in four packed accumulators
+            const float2 c2 = make_float2(C, C), n2 = make_float2(-m_run, -m_run);
+            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f)};
             uint32_t pk[BN / 2];
 #pragma unroll
             for (int c = 0; c < BN; c += 2) {
-                const float p0 = ex2(fmaf(__uint_as_float(sr[c]), C, neg));
-                const float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), C, neg));
-                ps += p0 + p1;
-                pk[c / 2] = pack_bf16(p0, p1);
+                const float2 x = ffma2(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2, n2);
+                const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+                acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pp);
+                pk[c / 2] = pack_bf16(pp.x, pp.y);
             }
-            l += ps;
+            const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
+            const float2 a = fadd2(a01, a23);
+            l += a.x + a.y;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t *rr = pk + 32 * c;

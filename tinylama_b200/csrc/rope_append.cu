@@ -91,8 +91,10 @@ __global__ void rope_append_kernel(const RopeAppendArgs a, const RopeTab tab) {
                     const int64_t i0 = v.at(b, t, hh, 2 * i), i1 = v.at(b, t, hh, 2 * i + 1);
                     float y0 = v.ptr[i0], y1 = v.ptr[i1];
                     if (rot) rotate_cs(y0, y1, c, sn, y0, y1);
-                    v.ptr[i0] = y0;
-                    v.ptr[i1] = y1;
+                    if (a.q_inplace) {
+                        v.ptr[i0] = y0;
+                        v.ptr[i1] = y1;
+                    }
                     if (a.qb) {
                         __nv_bfloat16 *qb = reinterpret_cast<__nv_bfloat16 *>(a.qb);
                         const int64_t o = (((int64_t)b * a.nHead + hh) * a.ntok + t) * a.headDim + 2 * i;
@@ -105,8 +107,10 @@ __global__ void rope_append_kernel(const RopeAppendArgs a, const RopeTab tab) {
                     float y0 = v.ptr[i0], y1 = v.ptr[i1];
                     if (a.rope_k && rot) {
                         rotate_cs(y0, y1, c, sn, y0, y1);
-                        v.ptr[i0] = y0;
-                        v.ptr[i1] = y1;
+                        if (a.k_inplace) {
+                            v.ptr[i0] = y0;
+                            v.ptr[i1] = y1;
+                        }
                     }
                     if (a.store) {
                         if (!in_range) {

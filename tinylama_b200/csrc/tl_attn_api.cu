@@ -162,7 +162,8 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
     long long want = (tot * h->nHeadKv + (long long)ctas * 4 - 1) / ((long long)ctas * 4);
     int chunk = (int)std::min<long long>(1024, std::max<long long>(32, want));
     chunk = (chunk + 31) / 32 * 32;
-    const int min_chunk = ((nmax + 255) / 256 + 31) / 32 * 32;  // at most 256 chunks/sequence
+    // at most 64 chunks per sequence: the last CTA of a sequence merges all of them
+    const int min_chunk = ((nmax + 63) / 64 + 31) / 32 * 32;
     chunk = std::max(chunk, min_chunk);
     long long units = 0;
     bool multi = false;
@@ -724,6 +725,9 @@ static int prefill_step_impl(tl_attn *h, int layer, int slot0, int nseq, int seq
     a.headDim = D;
     a.pos0_scalar = 0;
     a.rope_q = a.rope_k = a.store = true;
+    // the tensor-core path reads the bf16 copy of q and the cache, so the rotated fp32 q and k
+    // need not be written back
+    a.q_inplace = a.k_inplace = !tc;
     a.layer = layer;
     a.slot0 = slot0;
     a.qb = tc ? h->dQb : nullptr;
