@@ -345,6 +345,7 @@ def run_decode_batched(args, dist, kvd: int):
     }
     if not args.no_prefill:
         res["prefill"] = run_prefill(args, dist)
+        res["decode_tinyllama"] = run_decode_tiny(args, dist)
     if n == 1 and dist.rank == 0 and not args.no_cpu_baseline:
         rate, sample = cpu_decode_sample(w.lens, w.Hq, w.Hkv, w.D, w.base, args.cpu_budget, 1)
         res["cpu_baseline"] = {"value": round(rate, 3), "unit": "tok/s", "cores": 1, "kind": "port",
@@ -399,6 +400,78 @@ def run_prefill(args, dist):
     return {"workload": "causal prefill, 8 sequences, 32 q / 8 kv heads, head_dim 64, bf16 KV "
                         "(tcgen05), step = RoPE + cache write + attention",
             "by_seq_len": res, "peak_tflops": pk["bf16_tflops"], "peak_src": pk["src"]}
+
+
+# ------------------------------------------------------------- TinyLlama decode latency
+def run_decode_tiny(args, dist, Hq=32, Hkv=4, D=64, base=10000.0, lengths=(128, 512, 2048), nslots=64):
+    """TinyLlama GQA decode (32 q / 4 kv heads, head_dim 64, f32), batch 1: the cache holds L
+    positions, the query is the token at position L-1 (RoPE at L-1, append, attention over L).
+    1000 steps per length, replayed from a CUDA graph.  Two figures per length: the same cache
+    every step (it stays in L2: latency-bound) and a rotation over 64 distinct caches (64 x
+    2*4*L*64*4 B > L2 for L >= 2048) so that the K/V reads come from HBM."""
+    import torch
+    from tinylama_b200 import _lib
+    p = lambda t: C.c_void_p(t.data_ptr())
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = C.c_void_p(stream.cuda_stream)
+    steps = 1000
+    out = {}
+    for L in lengths:
+        h = C.c_void_p()
+        _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, base, L, nslots, 0,
+                                           torch.cuda.current_device()))
+        try:
+            g = torch.Generator(device="cuda").manual_seed(L)
+            for slot in range(nslots):
+                k = torch.randn(L, Hkv * D, device="cuda", generator=g)
+                v = torch.randn(L, Hkv * D, device="cuda", generator=g)
+                _lib.check(_lib.lib.tl_kv_store(h, 0, slot, 0, p(k), p(v), L, sp))
+            q = torch.randn(nslots, Hq * D, device="cuda", generator=g)
+            k1 = torch.randn(nslots, Hkv * D, device="cuda", generator=g)
+            v1 = torch.randn(nslots, Hkv * D, device="cuda", generator=g)
+            o = torch.empty(nslots, Hq * D, device="cuda")
+            pos_host = np.full(1, L - 1, np.int32)
+            pos = torch.from_numpy(pos_host).cuda()
+            ph = pos_host.ctypes.data_as(C.c_void_p)
+
+            def step(slot):
+                _lib.check(_lib.lib.tl_decode_step(h, 0, slot, 1, p(pos), ph, p(q[slot]), p(k1[slot]),
+                                                   p(v1[slot]), p(o[slot]), sp))
+
+            res = {}
+            for mode, slots in (("l2_resident", [0]), ("hbm_rotating_64", list(range(nslots)))):
+                for _ in range(3):
+                    for sl in slots:
+                        step(sl)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for sl in slots:
+                        step(sl)
+                reps = steps // len(slots)
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (reps * len(slots))
+                nbytes = 2 * Hkv * D * L * 4 + 2 * Hq * D * 4
+                res[mode] = {"us_per_step": round(us, 3), "tok_s": round(1e6 / us, 1),
+                             "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+                del graph
+            _lib.check(_lib.lib.tl_check_device(h, sp))
+            out[str(L)] = res
+        finally:
+            _lib.lib.tl_attn_destroy(h)
+    return {"workload": "TinyLlama GQA decode (32 q / 4 kv heads, head_dim 64, f32 KV), batch 1, "
+                        "1000 CUDA-graph steps per length; step = RoPE + append + attention",
+            "by_ctx_len": out, "bytes_per_step": "2048*L + 16384"}
 
 
 # ------------------------------------------------------------ long-context split-KV decode
@@ -508,7 +581,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_batched",
-                    choices=["decode_batched", "decode_batched_bf16", "splitkv", "prefill"])
+                    choices=["decode_batched", "decode_batched_bf16", "splitkv", "prefill", "decode_tiny"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the prefill sub-measurement")
     ap.add_argument("--prefill-sizes", default="512,2048,8192", help="sequence lengths of the prefill")
@@ -530,6 +603,8 @@ def main():
             res = run_decode_batched(args, dist, 1)
         elif args.workload == "splitkv":
             res = run_splitkv(args, dist)
+        elif args.workload == "decode_tiny":
+            res = run_decode_tiny(args, dist)
         else:
             res = run_prefill(args, dist)
         if dist.rank == 0:

@@ -334,8 +334,17 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     using C = DecCfg<KV, D, G>;
     const size_t smem = C::smem_bytes(a.nseq) + 4 * (size_t)a.nseq;
     auto kern = decode_kernel<KV, D, G>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    // set the shared-memory limit only when it grows, so that steady-state launches (and CUDA
+    // graph capture of them) make no attribute calls
+    static size_t smem_set[64] = {};  // per device: attributes are per context
+    int dev = 0;
+    cudaGetDevice(&dev);
+    size_t &cur = smem_set[dev & 63];
+    if (smem > cur) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        cur = smem;
+    }
     kern<<<num_ctas, C::THREADS, smem, s>>>(a);
     return cudaGetLastError();
 }

@@ -336,8 +336,16 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     if (!make_cache_map(&km, a.kv.k, rows, D) || !make_cache_map(&vm, a.kv.v, rows, D)) return cudaErrorNotSupported;
     const size_t smem = C::smem_bytes(a.nseq);
     auto kern = decode_mma_kernel<D, G>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    // only when it grows (per device): steady-state launches make no attribute calls
+    static size_t smem_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    size_t &cur = smem_set[dev & 63];
+    if (smem > cur) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        cur = smem;
+    }
     kern<<<num_ctas, C::THREADS, smem, s>>>(km, vm, a);
     return cudaGetLastError();
 }
