@@ -18,8 +18,8 @@ LIB = os.path.join(HERE, "liboracle.so")
 
 
 def build() -> str:
-    src = os.path.join(HERE, "attn_oracle.c")
-    if not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(src):
+    srcs = [os.path.join(HERE, f) for f in ("attn_oracle.c", "attn_ops_oracle.c", "attn_oracle.h")]
+    if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
     return LIB
 
@@ -45,6 +45,10 @@ def _load():
         fn.restype = None
     lib.ora_rope_theta.argtypes = [I, I, F]
     lib.ora_rope_theta.restype = F
+    lib.ora_attn_ops_create.argtypes = [I, I, I]
+    lib.ora_attn_ops_create.restype = P
+    lib.ora_attn_ops_destroy.argtypes = [P]
+    lib.ora_attn_ops_destroy.restype = None
     return lib
 
 

@@ -1,0 +1,69 @@
+"""End-to-end TinyLlama-architecture greedy decode with the attention on the B200.
+
+A llama GGUF is synthesised from a seed, with the TinyLlama-1.1B shapes:
+* 22 layers, dim 2048, 32 q-heads and 4 kv-heads, head_dim 64;
+* ffn 5632, vocab 32000, rope theta 1e4, rms eps 1e-5;
+* N(0, 0.02) weights quantised to Q2_K;
+* float32 RMSNorm weights of 1.0 and a float32 token embedding.
+
+The C++ host forward pass (libtlhost.so) then runs the reference's runPrompt twice: once with
+the B200 attention procs (libtlattn.so) and once with the oracle's.  The prompt is 8 random ids
+in [3, 32000) followed by 16 greedy tokens, batch 1.
+
+The generated ids must be identical.  Every attention output (each layer of the prefill and of
+each decode step) is compared.  Its inputs come from the run's own earlier layers, so it carries
+the upstream differences too; the bound on it is normwise.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import gguf_synth, oracle as ora
+from tests.helpers import max_rel_err, normwise_err
+
+pytestmark = pytest.mark.gpu
+
+TINYLLAMA = dict(nLayer=22, nEmb=2048, nHead=32, nHeadKv=4, nFfn=5632, nVocab=32000)
+SEED = 20261201
+
+
+@pytest.fixture(scope="module")
+def tinyllama(tmp_path_factory, cuda_lib):
+    from tinylama_b200.host_api import Model
+    path = str(tmp_path_factory.mktemp("gguf") / "tinyllama_synth.gguf")
+    gguf_synth.write_model(path, seed=SEED, **TINYLLAMA)
+    m = Model(path, nthreads=os.cpu_count() or 1)
+    yield m
+    m.close()
+
+
+def _chunks(hp, n_prompt, n_new):
+    hd = hp.nEmb // hp.nHead
+    sizes = [hp.nHead * hd * n_prompt] * hp.nLayer + [hp.nHead * hd] * (hp.nLayer * (n_new - 1))
+    return sizes
+
+
+def test_tinyllama_greedy_ids_identical(tinyllama):
+    from tinylama_b200 import host_api
+    m = tinyllama
+    prompt = np.random.default_rng(SEED).integers(3, 32000, size=8).astype(np.int32)
+    ops_o = ora.lib().ora_attn_ops_create(m.hp.nLayer, m.hp.nHeadKv, m.hp.nEmb // m.hp.nHead)
+    ops_g = host_api.gpu_attn_ops(m.hp)
+    try:
+        ids_o, gaps_o, dump_o = m.generate(ops_o, prompt, 16)
+        ids_g, gaps_g, dump_g = m.generate(ops_g, prompt, 16)
+    finally:
+        ora.lib().ora_attn_ops_destroy(ops_o)
+        host_api.free_gpu_attn_ops(ops_g)
+    worst_norm, worst_floor, off = 0.0, 0.0, 0
+    for size in _chunks(m.hp, 8, 16):
+        a, b = dump_g[off:off + size], dump_o[off:off + size]
+        worst_norm = max(worst_norm, normwise_err(a, b))
+        worst_floor = max(worst_floor, max_rel_err(a, b))
+        off += size
+    assert off == dump_o.size == dump_g.size
+    print(f"\nids {ids_g.tolist()}\nmin top-2 gap {gaps_o.min():.4f}; per-layer attention: "
+          f"normwise {worst_norm:.2e}, floored elementwise {worst_floor:.2e}")
+    assert worst_norm <= 1e-3, worst_norm
+    assert np.array_equal(ids_g, ids_o), (ids_g, ids_o, gaps_o)

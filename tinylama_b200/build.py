@@ -46,6 +46,25 @@ def _compile(src: str, verbose_ptxas: bool) -> str:
     return obj
 
 
+HOST_SRC = os.path.join(HERE, "host", "tl_host.cpp")
+HOST_LIB = os.path.join(HERE, "libtlhost.so")
+CXX = os.environ.get("CXX", "g++")
+
+
+def build_host() -> str:
+    """libtlhost.so: the C++ host forward pass (CPU linears) over libtlattn.so's attention.
+    -ffp-contract=off keeps the reference's float32 rounding (no fused multiply-adds)."""
+    deps = [HOST_SRC, os.path.join(ROOT, "include", "tl_host.h"), os.path.join(ROOT, "include", "tl_attn.h"), LIB]
+    if os.path.exists(HOST_LIB) and os.path.getmtime(HOST_LIB) >= max(os.path.getmtime(d) for d in deps):
+        return HOST_LIB
+    cmd = [CXX, "-O2", "-ffp-contract=off", "-fno-fast-math", "-std=c++17", "-fPIC", "-shared", "-pthread",
+           "-fvisibility=hidden", HOST_SRC, "-o", HOST_LIB, "-L" + HERE, "-ltlattn", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host build failed:\n{r.stdout}\n{r.stderr}")
+    return HOST_LIB
+
+
 def build(verbose_ptxas: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
@@ -55,6 +74,7 @@ def build(verbose_ptxas: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_host()
     return LIB
 
 
