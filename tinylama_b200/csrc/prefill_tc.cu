@@ -223,6 +223,7 @@ struct Bars {
 // Per KV tile j and query tile q the MMA issuer runs S_q(j+1) = Q_q K_{j+1}^T as soon as the
 // softmax group has pulled S_q(j) into registers (s_free), and O_q += P_q(j) V_j once P_q(j) is
 // in TMEM (p_ready), so the tensor core works on one tile while the other group's softmax runs.
+// A group overwrites P_q and rescales O_q only after PV_q(j-1) has completed (o_bar).
 __global__ void __launch_bounds__(THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap, const TcParams p) {
@@ -358,28 +359,43 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, p.err, abort_flag));
             if (!ok) break;
             tc_fence_after();
+            // S in two halves: the second half's TMEM load overlaps the first half's maximum
             uint32_t sr[BN];
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t *rr = sr + 32 * c;
-                TL_LD32(tmem + lane_base + col_s(q) + 32 * c, rr);
-            }
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
             const int k0 = j * BN;
-            if (j == nt[q] - 1) {  // diagonal / ragged tile: causal and length mask
-#pragma unroll
-                for (int c = 0; c < BN; ++c)
-                    if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
-            }
-            // row maximum: four independent chains of three-input max
+            const bool diag = (j == nt[q] - 1);  // diagonal / ragged tile: causal and length mask
             float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < BN; c += 8) {
+            for (int half = 0; half < 2; ++half) {
+                if (half == 0) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    mq[u] = max3f(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t *rr = sr + 32 * c;
+                        TL_LD32(tmem + lane_base + col_s(q) + 32 * c, rr);
+                    }
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int c = 2; c < 4; ++c) {
+                        uint32_t *rr = sr + 32 * c;
+                        TL_LD32(tmem + lane_base + col_s(q) + 32 * c, rr);
+                    }
+                } else {
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
+                }
+                const int c0 = half * (BN / 2);
+                if (diag) {
+#pragma unroll
+                    for (int c = c0; c < c0 + BN / 2; ++c)
+                        if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
+                }
+                // row maximum: four independent chains of three-input max
+#pragma unroll
+                for (int c = c0; c < c0 + BN / 2; c += 8) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        mq[u] = max3f(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+                }
             }
             const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
             const float ms = mx * C;
@@ -390,11 +406,14 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 m_run = ms;
                 l *= alpha;
             }
-            if (__any_sync(0xffffffffu, grow && j > 0)) {
-                // O_q holds the sum through tile j-1; wait for that PV, then rescale in TMEM
+            if (j > 0) {
+                // PV_q(j-1) must be complete before P_q is overwritten (and before O_q is rescaled)
                 ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_bar[q], (j - 1) & 1, p.err, abort_flag));
                 if (!ok) break;
                 tc_fence_after();
+            }
+            if (__any_sync(0xffffffffu, grow && j > 0)) {
+                // O_q holds the sum through tile j-1: rescale it in TMEM
 #pragma unroll
                 for (int c = 0; c < HD / 16; ++c) {  // 16 columns at a time: S stays in registers
                     uint32_t orr[16];
