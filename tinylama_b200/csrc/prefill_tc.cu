@@ -5,17 +5,20 @@
 // Inputs are bf16 (Q staged by the RoPE kernel, K/V from the cache the same launch sequence
 // appended to), products accumulate in fp32 in tensor memory, softmax runs in fp32.
 //
-// One CTA owns 256 query rows (two tiles of 128) of one (sequence, q-head).  A TMA warp brings
-// Q once and K/V tiles of 128 positions (2-D tensor maps, 128-byte swizzle, no multicast) into a
-// three-deep ring; a single MMA thread issues S_q = Q_q K^T (4 x tcgen05.mma kind::f16, M=128,
-// N=128, K=16, A and B K-major from shared memory) and O_q += P_q V (8 MMAs, A = P from TMEM,
-// B = V MN-major from shared memory); two softmax groups of 128 threads (thread = query row =
-// TMEM lane) load S, mask causally, keep the online max/sum in fp32 (log2 domain), write P as
-// packed bf16 into TMEM and rescale O in TMEM only when a row's maximum grows past 2^8.  S and
-// P have separate TMEM columns, so S_q(j+1) runs on the tensor core while the softmax of
-// S_q(j) is still in flight, and the two query tiles alternate.  KV tiles past the diagonal are
-// skipped.  Every mbarrier wait is bounded (common.cuh); TMEM is released on every exit path
-// after the MMA thread has seen its own last commit.
+// One CTA owns NQ x 128 query rows (NQ = 2: two tiles of 128) of one (sequence, q-head).  A TMA
+// warp brings Q once and K/V tiles of BN = 128 positions (2-D tensor maps, 128-byte swizzle, no
+// multicast) into a three-deep ring.  tcgen05.mma issue is spread over three warps of the control
+// warpgroup, each a converged warp with one elected lane issuing: one issues S_q = Q_q K^T
+// (4 x kind::f16, M=128, N=128, K=16, A and B K-major from shared memory), two issue O_q += P_q V
+// (A = P from TMEM, B = V MN-major from shared memory).  Issuing an MMA occupies the issuing
+// warp's scheduler partition, and spreading it keeps the four softmax warps of a group in step.
+// NQ softmax warpgroups (thread = query row = TMEM lane) load S, mask causally, keep the online
+// max/sum in fp32 (log2 domain), write P as packed bf16 into TMEM and rescale O in TMEM only
+// when a row's maximum grows past 2^8.  One pair in four of the exponentials runs as a
+// polynomial on the FMA pipe, the rest on MUFU.  S and P have separate TMEM columns, so
+// S_q(j+1) runs on the tensor core while the softmax of S_q(j) is still in flight.  KV tiles
+// past the diagonal are skipped.  Every mbarrier wait is bounded (common.cuh); TMEM is released
+// on every exit path after all issued MMAs have completed.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -29,18 +32,19 @@ namespace tl {
 namespace {
 
 constexpr int BM = 128;             // query rows per CTA
-constexpr int BN = 128;             // keys per KV tile
 constexpr int HD = 64;              // head_dim covered by this kernel
 constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB, one 128 x 64 bf16 tile
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ---- PTX wrappers ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y,
-                                            uint64_t *bar) {
+                                            uint64_t *bar, uint32_t issue) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+        "{\n\t.reg .pred e;\n\t"
+        "setp.ne.b32 e, %5, 0;\n\t"
+        "@e cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n\t}" ::
             "r"(smem_u32(smem_dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "r"(issue)
         : "memory");
 }
 
@@ -61,28 +65,61 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-// D[tmem] (+)= A[smem desc] * B[smem desc]
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
+// One lane of a converged warp is elected to issue; the rest of the warp runs the same code with
+// the instruction predicated off.  Keeping the issuing warp converged lets the compiler hold the
+// descriptors in uniform registers instead of moving them lane by lane around every issue.
+__device__ __forceinline__ uint32_t elect_one() {
+    uint32_t e;
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, e;\n\t}"
+        : "=r"(e));
+    return e;
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar, uint32_t issue) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "setp.ne.b32 e, %1, 0;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
+        "r"(issue)
         : "memory");
 }
-// D[tmem] (+)= A[tmem] * B[smem desc]
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
+// S = Q K^T for one 128 x BN tile, K = 64 as four K=16 MMAs in one block: the predicates are set
+// once and the descriptors step by 32 bytes (the K=16 slice of a 128-byte swizzled row), so the
+// issuing warp spends a few instructions per MMA.
+__device__ __forceinline__ void mma_s_k64(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t issue) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred e, t, f;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+        "setp.ne.b32 e, %4, 0;\n\t"
+        "setp.eq.b32 t, %4, %4;\n\t"
+        "setp.ne.b32 f, %4, %4;\n\t"
+        "add.s64 a1, %1, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 a3, %1, 6;\n\t"
+        "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, f;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, t;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(issue)
+        : "memory");
+}
+// O += P V over 64 keys: four K=16 MMAs, A = P from TMEM (8 columns of packed bf16 per step), B = V
+// MN-major from shared memory (16 rows of 128 bytes = 2048 bytes per step).
+__device__ __forceinline__ void mma_pv_k64(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate, uint32_t issue) {
+    asm volatile(
+        "{\n\t.reg .pred e, t, p;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+        "setp.ne.b32 e, %5, 0;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        "setp.eq.b32 t, %5, %5;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.s64 b1, %2, 128;\n\tadd.s64 b2, %2, 256;\n\tadd.s64 b3, %2, 384;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, t;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
         : "memory");
 }
 
@@ -164,20 +201,36 @@ struct TcParams {
     unsigned *err;
 };
 
-constexpr int NS_KV = 3;                       // K/V ring depth (32 KB per stage)
-constexpr int THREADS = 384;                   // 3 warpgroups: control, softmax tile 0, softmax tile 1
-constexpr int TMEM_ALL = 512;
-// TMEM columns: S0 | S1 | P0 | P1 | O0 | O1
-__host__ __device__ constexpr int col_s(int q) { return q * 128; }
-__host__ __device__ constexpr int col_p(int q) { return 256 + q * 64; }
-__host__ __device__ constexpr int col_o(int q) { return 384 + q * 64; }
-constexpr float kRescaleThreshold = 8.0f;      // log2 units: O is rescaled only past 2^8
+// Kernel shape: NQ query tiles of 128 rows per CTA and KV tiles of BN positions.  One control
+// warpgroup (TMA warp, MMA warp) and NQ softmax warpgroups; each scheduler partition holds one
+// control warp and NQ softmax warps, and more softmax warps per partition hide more latency.
+// TMEM per query tile: S (BN columns) + P (BN/2, packed bf16) + O (64).
+template <int NQ, int BN_>
+struct TcShape {
+    static constexpr int THREADS = 128 * (NQ + 1);
+    static constexpr int KV_TILE = BN_ * HD * 2;                      // bytes of one K or V tile
+    static constexpr int NS = (96 * 1024) / (2 * KV_TILE);            // K/V ring depth: 96 KB
+    static constexpr int REG_LAUNCH = (65536 / THREADS) / 8 * 8;       // 168 (NQ=2) / 128 (NQ=3)
+    static constexpr int REG_CTRL = NQ == 2 ? 104 : 80;
+    static constexpr int REG_SOFT = NQ == 2 ? 200 : 144;
+    static_assert(REG_CTRL + NQ * REG_SOFT <= (NQ + 1) * REG_LAUNCH, "register split exceeds the launch allotment");
+    static constexpr int COL_P0 = NQ * BN_;
+    static constexpr int COL_O0 = COL_P0 + NQ * BN_ / 2;
+    static_assert(COL_O0 + NQ * 64 <= 512, "TMEM columns");
+    __host__ __device__ static constexpr int col_s(int q) { return q * BN_; }
+    __host__ __device__ static constexpr int col_p(int q) { return COL_P0 + q * (BN_ / 2); }
+    __host__ __device__ static constexpr int col_o(int q) { return COL_O0 + q * 64; }
+    static constexpr int SMEM = NQ * TILE_BYTES + NS * 2 * KV_TILE;  // + barriers
+};
 
-// Each scheduler partition runs one control warp and two softmax warps (warp w sits on
-// partition w % 4).  Registers move from the control warpgroup (104 per thread) to the softmax
-// groups (200): 104 + 2*200 = 504 = 3*168, the allotment of three warps launched at 168.
-__device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 104;"); }
-__device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 200;"); }
+constexpr int TMEM_ALL = 512;
+constexpr int kIssuers = 3;  // warps that issue tcgen05.mma: one for S, two for P V
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only past 2^8
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
     float r;
@@ -208,62 +261,112 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^x for a pair on the FMA pipe, to take part of the exponentials off the MUFU unit (whose
+// throughput, 16 per SM per clock, bounds this kernel).  Range reduction by the round-to-nearest
+// magic constant 1.5 * 2^23: t = x + M keeps n = round(x) in its low mantissa bits, f = x - n lies
+// in [-0.5, 0.5], 2^f comes from a degree-3 polynomial fitted for minimax relative error on that
+// interval (7.5e-5 relative, below the bf16 rounding of P), and 2^n is added to the exponent
+// field.  x is clamped to -125 so that the exponent never underflows (2^-125 stands in for 0).
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long *>(&a)), "l"(*reinterpret_cast<unsigned long long *>(&b)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long *>(&a)), "l"(*reinterpret_cast<unsigned long long *>(&b)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    constexpr float kM = 12582912.0f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -125.f);
+    x.y = fmaxf(x.y, -125.f);
+    const float2 t = fadd2_rn(x, make_float2(kM, kM));
+    const float2 f = fsub2(x, fsub2(t, make_float2(kM, kM)));
+    float2 p = ffma2(make_float2(0.05517132207751274f, 0.05517132207751274f), f,
+                     make_float2(0.24261054396629333f, 0.24261054396629333f));
+    p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    p = ffma2(p, f, make_float2(0.9999281167984009f, 0.9999281167984009f));
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
 
+#ifndef TL_POLY_MOD
+#define TL_POLY_MOD 4
+#endif
+// every TL_POLY_MOD-th pair of a row's exponentials runs on the FMA pipe (0: none)
+constexpr int kPolyMod = TL_POLY_MOD;
+
+template <int NQ, int NS>
 struct Bars {
-    uint64_t q_full, kv_full[NS_KV], kv_empty[NS_KV], s_full[2], s_free[2], p_ready[2], o_bar[2],
-        o_done[2], mma_final;
+    uint64_t q_full, kv_full[NS], kv_empty[NS], s_full[NQ], s_free[NQ], p_ready[NQ], o_bar[NQ], o_done[NQ],
+        mma_final;
     uint32_t tmem_base;
     int abort;
 };
 
-// Causal prefill, one CTA = 256 query rows (two 128-row tiles) of one (sequence, q-head).
+// Causal prefill, one CTA = NQ*128 query rows of one (sequence, q-head).
 //   warpgroup 0: warp 0 lane 0 = TMA producer; warp 1 = TMEM owner, its lane 0 the MMA issuer
-//   warpgroups 1 / 2: softmax of query tile 0 / 1, thread = row = TMEM lane (warp w reaches
-//   TMEM lanes 32*(w%4)..)
-// Per KV tile j and query tile q the MMA issuer runs S_q(j+1) = Q_q K_{j+1}^T as soon as the
-// softmax group has pulled S_q(j) into registers (s_free), and O_q += P_q(j) V_j once P_q(j) is
-// in TMEM (p_ready), so the tensor core works on one tile while the other group's softmax runs.
-// A group overwrites P_q and rescales O_q only after PV_q(j-1) has completed (o_bar).
-__global__ void __launch_bounds__(THREADS, 1)
+//   warpgroup 1+q: softmax of query tile q, thread = row = TMEM lane (warp w reaches TMEM lanes
+//   32*(w%4)..)
+// Per KV tile j and query tile q the MMA issuer runs S_q(j+1) = Q_q K_{j+1}^T as soon as group q
+// has pulled S_q(j) into registers (s_free), and O_q += P_q(j) V_j once P_q(j) is in TMEM
+// (p_ready), so the tensor core works on one tile while the other groups' softmax runs.  A group
+// overwrites P_q and rescales O_q only after PV_q(j-1) has completed (o_bar).
+template <int NQ, int BN_>
+__global__ void __launch_bounds__(TcShape<NQ, BN_>::THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap, const TcParams p) {
+    using S_ = TcShape<NQ, BN_>;
+    constexpr int BNK = BN_;
+    constexpr int NS = S_::NS;
+    using B_ = Bars<NQ, NS>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-    uint8_t *sQ[2] = {base, base + TILE_BYTES};
-    uint8_t *sK = base + 2 * TILE_BYTES;                  // [NS_KV] tiles
-    uint8_t *sV = base + (2 + NS_KV) * TILE_BYTES;        // [NS_KV] tiles
-    Bars *bars = reinterpret_cast<Bars *>(base + (2 + 2 * NS_KV) * TILE_BYTES);
+    uint8_t *sQ = base;                                  // [NQ] 16 KB tiles
+    uint8_t *sK = base + NQ * TILE_BYTES;                // [NS] tiles
+    uint8_t *sV = sK + NS * S_::KV_TILE;                 // [NS] tiles
+    B_ *bars = reinterpret_cast<B_ *>(sV + NS * S_::KV_TILE);
     volatile int *abort_flag = &bars->abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int npairs = (p.ntok + 2 * BM - 1) / (2 * BM);
-    const int pair = npairs - 1 - (int)blockIdx.x;  // heavy (late) tiles first
+    const int ngroups = (p.ntok + NQ * BM - 1) / (NQ * BM);
+    const int grp = ngroups - 1 - (int)blockIdx.x;  // heavy (late) tiles first
     const int h = blockIdx.y, b = blockIdx.z;
     const int g = h / (p.nHead / p.nHeadKv);
-    const int q0 = pair * 2 * BM;
-    int nt[2];
+    const int q0 = grp * NQ * BM;
+    int nt[NQ];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
+    for (int q = 0; q < NQ; ++q) {
         const int start = q0 + q * BM;
-        nt[q] = start < p.ntok ? (min(start + BM, p.ntok) + BN - 1) / BN : 0;
+        nt[q] = start < p.ntok ? (min(start + BM, p.ntok) + BNK - 1) / BNK : 0;
     }
-    const int nkv = max(nt[0], nt[1]);
+    int nkv = 0, nq_live = 0;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+        nkv = max(nkv, nt[q]);
+        nq_live += nt[q] > 0;
+    }
 
     if (tid == 0) {
         mbar_init(&bars->q_full, 1);
-        for (int i = 0; i < NS_KV; ++i) {
+        for (int i = 0; i < NS; ++i) {
             mbar_init(&bars->kv_full[i], 1);
-            mbar_init(&bars->kv_empty[i], 1);
+            mbar_init(&bars->kv_empty[i], kIssuers);
         }
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < NQ; ++q) {
             mbar_init(&bars->s_full[q], 1);
             mbar_init(&bars->s_free[q], BM);
             mbar_init(&bars->p_ready[q], BM);
             mbar_init(&bars->o_bar[q], 1);
             mbar_init(&bars->o_done[q], 1);
         }
-        mbar_init(&bars->mma_final, 1);
+        mbar_init(&bars->mma_final, kIssuers);
         bars->abort = 0;
         fence_mbar_init();
     }
@@ -279,77 +382,97 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     const int kvrow0 = (int)(p.kv_row_layer + (int64_t)b * p.kv_rows_per_slot + (int64_t)g * p.maxLen);
 
     if (warp < 4) {
-        setmaxnreg_dec();
-        if (warp == 0 && lane == 0) {
-            // ---------------- TMA producer ----------------
-            mbar_arrive_expect_tx(&bars->q_full, (nt[1] > 0 ? 2 : 1) * TILE_BYTES);
-            tma_load_2d(sQ[0], &qmap, 0, qrow, &bars->q_full);
-            if (nt[1] > 0) tma_load_2d(sQ[1], &qmap, 0, qrow + BM, &bars->q_full);
+        setmaxnreg_dec<S_::REG_CTRL>();
+        // bounded wait by the whole warp with a warp-uniform verdict
+        auto wait_all = [&](uint64_t *bar, uint32_t parity, unsigned *err, volatile int *ab) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, ab));
+        };
+        if (warp == 0) {
+            // ---------------- TMA producer (one elected lane issues) ----------------
+            const uint32_t leader = elect_one();
+            if (leader) mbar_arrive_expect_tx(&bars->q_full, nq_live * TILE_BYTES);
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < NQ; ++q)
+                if (nt[q] > 0) tma_load_2d(sQ + q * TILE_BYTES, &qmap, 0, qrow + q * BM, &bars->q_full, leader);
             int issued = 0;
-            bool ok = true;
-            for (int j = 0; j < nkv && ok; ++j) {
-                const int st = j % NS_KV;
-                if (!mbar_wait(&bars->kv_empty[st], ((j / NS_KV) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
-                mbar_arrive_expect_tx(&bars->kv_full[st], 2 * TILE_BYTES);
-                tma_load_2d(sK + st * TILE_BYTES, &kmap, 0, kvrow0 + j * BN, &bars->kv_full[st]);
-                tma_load_2d(sV + st * TILE_BYTES, &vmap, 0, kvrow0 + j * BN, &bars->kv_full[st]);
+            for (int j = 0; j < nkv; ++j) {
+                const int st = j % NS;
+                if (!wait_all(&bars->kv_empty[st], ((j / NS) & 1) ^ 1, p.err, abort_flag)) break;
+                if (leader) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * S_::KV_TILE);
+                __syncwarp();
+                tma_load_2d(sK + st * S_::KV_TILE, &kmap, 0, kvrow0 + j * BNK, &bars->kv_full[st], leader);
+                tma_load_2d(sV + st * S_::KV_TILE, &vmap, 0, kvrow0 + j * BNK, &bars->kv_full[st], leader);
                 ++issued;
             }
             // wait (bounded) until every copy issued into this CTA's shared memory has landed
-            mbar_wait(&bars->q_full, 0, nullptr, nullptr);
-            for (int j = max(0, issued - NS_KV); j < issued; ++j)
-                mbar_wait(&bars->kv_full[j % NS_KV], (j / NS_KV) & 1, nullptr, nullptr);
-        } else if (warp == 1 && lane == 0) {
-            // ---------------- MMA issuer ----------------
-            const uint32_t idesc_s = idesc_bf16(BN, false);
-            const uint32_t idesc_o = idesc_bf16(HD, true);
-            bool ok = mbar_wait(&bars->q_full, 0, p.err, abort_flag) &&
-                      mbar_wait(&bars->kv_full[0], 0, p.err, abort_flag);
-            auto issue_s = [&](int q, int j) {
-                const uint32_t qa = smem_u32(sQ[q]), ka = smem_u32(sK + (j % NS_KV) * TILE_BYTES);
-#pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk)
-                    mma_ss(tmem + col_s(q), sw128_desc(qa + kk * 32, 16), sw128_desc(ka + kk * 32, 16), idesc_s,
-                           kk > 0 ? 1u : 0u);
-                tc_commit(&bars->s_full[q]);
-            };
-            if (ok) {
-                tc_fence_after();
-                for (int q = 0; q < 2; ++q)
-                    if (nt[q] > 0) issue_s(q, 0);
-            }
+            wait_all(&bars->q_full, 0, nullptr, nullptr);
+            for (int j = max(0, issued - NS); j < issued; ++j)
+                wait_all(&bars->kv_full[j % NS], (j / NS) & 1, nullptr, nullptr);
+        } else if (warp == 1) {
+            // ---------------- S issuer: S_q(j) = Q_q K_j^T ----------------
+            // Issuing a tcgen05.mma holds the issuing warp's scheduler for a while, so the MMAs
+            // are spread over three warps (three scheduler partitions): this one issues every S,
+            // warps 2 and 3 issue O += P V.
+            const uint32_t leader = elect_one();
+            const uint32_t idesc_s = idesc_bf16(BNK, false);
+            bool ok = wait_all(&bars->q_full, 0, p.err, abort_flag);
             for (int j = 0; j < nkv && ok; ++j) {
-                for (int q = 0; q < 2 && ok; ++q) {
-                    if (j >= nt[q]) continue;
-                    if (j + 1 < nt[q]) {
-                        ok = mbar_wait(&bars->s_free[q], j & 1, p.err, abort_flag) &&
-                             mbar_wait(&bars->kv_full[(j + 1) % NS_KV], ((j + 1) / NS_KV) & 1, p.err, abort_flag);
-                        if (!ok) break;
-                        tc_fence_after();
-                        issue_s(q, j + 1);
-                    }
-                    if (!mbar_wait(&bars->p_ready[q], j & 1, p.err, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t va = smem_u32(sV + (j % NS_KV) * TILE_BYTES);
+                ok = wait_all(&bars->kv_full[j % NS], (j / NS) & 1, p.err, abort_flag);
+                if (!ok) break;
+                const uint32_t ka = smem_u32(sK + (j % NS) * S_::KV_TILE);
 #pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk)
-                        mma_ts(tmem + col_o(q), tmem + col_p(q) + kk * 8, sw128_desc(va + kk * 2048, TILE_BYTES),
-                               idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(&bars->o_bar[q]);
-                    if (j == nt[q] - 1) tc_commit(&bars->o_done[q]);
+                for (int q = 0; q < NQ; ++q) {
+                    if (!ok || j >= nt[q]) continue;
+                    // S_q(j-1) must be in the softmax group's registers before it is overwritten
+                    if (j > 0) ok = wait_all(&bars->s_free[q], (j - 1) & 1, p.err, abort_flag);
+                    if (!ok) continue;
+                    tc_fence_after();
+                    mma_s_k64(tmem + S_::col_s(q), sw128_desc(smem_u32(sQ + q * TILE_BYTES), 16), sw128_desc(ka, 16),
+                              idesc_s, leader);
+                    tc_commit(&bars->s_full[q], leader);
                 }
-                if (ok) tc_commit(&bars->kv_empty[j % NS_KV]);
+                tc_commit(&bars->kv_empty[j % NS], leader);  // K_j is free once these S MMAs complete
             }
-            // every MMA this thread issued has completed before TMEM can be released
-            tc_commit(&bars->mma_final);
-            mbar_wait(&bars->mma_final, 0, p.err, nullptr);
+            // every MMA of the CTA has completed before TMEM can be released
+            tc_commit(&bars->mma_final, leader);
+            wait_all(&bars->mma_final, 0, p.err, nullptr);
+        } else {
+            // ---------------- PV issuers: O_q += P_q(j) V_j for q = warp - 2, warp, ... ----------------
+            const uint32_t leader = elect_one();
+            const uint32_t idesc_o = idesc_bf16(HD, true);
+            bool ok = true;
+            for (int j = 0; j < nkv && ok; ++j) {
+                // tile j's phase of kv_full has completed, so this warp's kv_empty arrival below
+                // belongs to tile j even when it issues nothing for it
+                ok = wait_all(&bars->kv_full[j % NS], (j / NS) & 1, p.err, abort_flag);
+                if (!ok) break;
+                const uint32_t va = smem_u32(sV + (j % NS) * S_::KV_TILE);
+#pragma unroll
+                for (int q = 0; q < NQ; ++q) {
+                    if (!ok || (q & 1) != warp - 2 || j >= nt[q]) continue;
+                    ok = wait_all(&bars->p_ready[q], j & 1, p.err, abort_flag);
+                    if (!ok) continue;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kb = 0; kb < BNK / 64; ++kb)
+                        mma_pv_k64(tmem + S_::col_o(q), tmem + S_::col_p(q) + kb * 32,
+                                   sw128_desc(va + kb * 4 * 2048, S_::KV_TILE), idesc_o, (j > 0 || kb > 0) ? 1u : 0u,
+                                   leader);
+                    tc_commit(&bars->o_bar[q], leader);
+                    if (j == nt[q] - 1) tc_commit(&bars->o_done[q], leader);
+                }
+                tc_commit(&bars->kv_empty[j % NS], leader);  // V_j is free once these PV MMAs complete
+            }
+            tc_commit(&bars->mma_final, leader);
         }
     } else {
-        setmaxnreg_inc();
+        setmaxnreg_inc<S_::REG_SOFT>();
         // ---------------- softmax of query tile q ----------------
         const int q = (warp - 4) >> 2;
         const int r = (warp & 3) * 32 + lane;
         const int row = q0 + q * BM + r;
+        const int row_first = q0 + q * BM;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const float C = kLog2e / 8.0f;  // log2(e) / sqrt(64)
         float m_run = -INFINITY, l = 0.f;
@@ -359,43 +482,28 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, p.err, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            // S in two halves: the second half's TMEM load overlaps the first half's maximum
-            uint32_t sr[BN];
-            const int k0 = j * BN;
-            const bool diag = (j == nt[q] - 1);  // diagonal / ragged tile: causal and length mask
+            uint32_t sr[BNK];
+#pragma unroll
+            for (int c = 0; c < BNK / 32; ++c) {
+                uint32_t *rr = sr + 32 * c;
+                TL_LD32(tmem + lane_base + S_::col_s(q) + 32 * c, rr);
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
+            const int k0 = j * BNK;
+            if (k0 + BNK - 1 > row_first || k0 + BNK > p.ntok) {  // tile crosses the diagonal or the end
+#pragma unroll
+                for (int c = 0; c < BNK; ++c)
+                    if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
+            }
+            // row maximum: four independent chains of three-input max
             float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                if (half == 0) {
+            for (int c = 0; c < BNK; c += 8) {
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        uint32_t *rr = sr + 32 * c;
-                        TL_LD32(tmem + lane_base + col_s(q) + 32 * c, rr);
-                    }
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int c = 2; c < 4; ++c) {
-                        uint32_t *rr = sr + 32 * c;
-                        TL_LD32(tmem + lane_base + col_s(q) + 32 * c, rr);
-                    }
-                } else {
-                    tmem_wait_ld();
-                    tc_fence_before();
-                    mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
-                }
-                const int c0 = half * (BN / 2);
-                if (diag) {
-#pragma unroll
-                    for (int c = c0; c < c0 + BN / 2; ++c)
-                        if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
-                }
-                // row maximum: four independent chains of three-input max
-#pragma unroll
-                for (int c = c0; c < c0 + BN / 2; c += 8) {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        mq[u] = max3f(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
-                }
+                for (int u = 0; u < 4; ++u)
+                    mq[u] = max3f(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
             }
             const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
             const float ms = mx * C;
@@ -413,26 +521,28 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 tc_fence_after();
             }
             if (__any_sync(0xffffffffu, grow && j > 0)) {
-                // O_q holds the sum through tile j-1: rescale it in TMEM
+                // O_q holds the sum through tile j-1: rescale it in TMEM, 16 columns at a time
 #pragma unroll
-                for (int c = 0; c < HD / 16; ++c) {  // 16 columns at a time: S stays in registers
+                for (int c = 0; c < HD / 16; ++c) {
                     uint32_t orr[16];
-                    TL_LD16(tmem + lane_base + col_o(q) + 16 * c, orr);
+                    TL_LD16(tmem + lane_base + S_::col_o(q) + 16 * c, orr);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 16; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-                    TL_ST16(tmem + lane_base + col_o(q) + 16 * c, orr);
+                    TL_ST16(tmem + lane_base + S_::col_o(q) + 16 * c, orr);
                 }
             }
             // p = 2^(s*C - m): the argument in packed pairs, the sum in four packed accumulators
             const float2 c2 = make_float2(C, C), n2 = make_float2(-m_run, -m_run);
             float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                              make_float2(0.f, 0.f)};
-            uint32_t pk[BN / 2];
+            uint32_t pk[BNK / 2];
 #pragma unroll
-            for (int c = 0; c < BN; c += 2) {
+            for (int c = 0; c < BNK; c += 2) {
                 const float2 x = ffma2(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2, n2);
-                const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+                const float2 pp = (kPolyMod > 0 && (c >> 1) % (kPolyMod > 0 ? kPolyMod : 1) == (kPolyMod > 0 ? kPolyMod : 1) - 1)
+                                      ? exp2_poly2(x)
+                                      : make_float2(ex2(x.x), ex2(x.y));
                 acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pp);
                 pk[c / 2] = pack_bf16(pp.x, pp.y);
             }
@@ -440,9 +550,9 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             const float2 a = fadd2(a01, a23);
             l += a.x + a.y;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            for (int c = 0; c < BNK / 64; ++c) {
                 uint32_t *rr = pk + 32 * c;
-                TL_ST32(tmem + lane_base + col_p(q) + 32 * c, rr);
+                TL_ST32(tmem + lane_base + S_::col_p(q) + 32 * c, rr);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -455,7 +565,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
 #pragma unroll
             for (int c = 0; c < HD / 32; ++c) {
                 uint32_t *rr = orr + 32 * c;
-                TL_LD32(tmem + lane_base + col_o(q) + 32 * c, rr);
+                TL_LD32(tmem + lane_base + S_::col_o(q) + 32 * c, rr);
             }
             tmem_wait_ld();
             if (row < p.ntok) {
@@ -498,12 +608,12 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
-bool make_map(CUtensorMap *m, const void *ptr, uint64_t rows) {
+bool make_map(CUtensorMap *m, const void *ptr, uint64_t rows, int box_rows) {
     auto enc = get_encode();
     if (!enc) return false;
     cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
-    cuuint32_t box[2] = {(cuuint32_t)HD, (cuuint32_t)BM};
+    cuuint32_t box[2] = {(cuuint32_t)HD, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -511,19 +621,15 @@ bool make_map(CUtensorMap *m, const void *ptr, uint64_t rows) {
     return r == CUDA_SUCCESS;
 }
 
-}  // namespace
-
-cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s) {
-    static_assert(BM == BN, "one tensor map box serves Q, K and V tiles");
-    if (a.headDim != HD || a.kv.dtype != TL_KV_BF16 || a.qb == nullptr || a.pos0 != nullptr ||
-        a.kf.ptr != nullptr)
-        return cudaErrorNotSupported;
+template <int NQ, int BN_>
+cudaError_t launch_shape(const PrefillArgs &a, cudaStream_t s) {
+    using S_ = TcShape<NQ, BN_>;
     const int64_t q_rows = (int64_t)a.nseq * a.nHead * a.ntok;
     const int64_t kv_rows = (int64_t)a.kv.nLayer * a.kv.maxBatch * a.kv.nHeadKv * a.kv.maxLen;
-    if (q_rows + 2 * BM > INT32_MAX || kv_rows + BN > INT32_MAX) return cudaErrorNotSupported;
+    if (q_rows + NQ * BM > INT32_MAX || kv_rows + BN_ > INT32_MAX) return cudaErrorNotSupported;
     CUtensorMap qm, km, vm;
-    if (!make_map(&qm, a.qb, (uint64_t)q_rows) || !make_map(&km, a.kv.k, (uint64_t)kv_rows) ||
-        !make_map(&vm, a.kv.v, (uint64_t)kv_rows))
+    if (!make_map(&qm, a.qb, (uint64_t)q_rows, BM) || !make_map(&km, a.kv.k, (uint64_t)kv_rows, BN_) ||
+        !make_map(&vm, a.kv.v, (uint64_t)kv_rows, BN_))
         return cudaErrorNotSupported;
     TcParams p;
     p.out = a.out;
@@ -535,12 +641,36 @@ cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s) {
     p.kv_rows_per_slot = a.kv.nHeadKv * a.kv.maxLen;
     p.maxLen = a.kv.maxLen;
     p.err = a.err;
-    const int smem = (2 + 2 * NS_KV) * TILE_BYTES + (int)sizeof(Bars) + 1024;
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid((a.ntok + 2 * BM - 1) / (2 * BM), a.nHead, a.nseq);
-    prefill_tc_kernel<<<grid, THREADS, smem, s>>>(qm, km, vm, p);
+    const int smem = S_::SMEM + (int)sizeof(Bars<NQ, S_::NS>) + 1024;
+    auto kern = prefill_tc_kernel<NQ, BN_>;
+    static int smem_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem_set[dev & 63] < smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        smem_set[dev & 63] = smem;
+    }
+    dim3 grid((a.ntok + NQ * BM - 1) / (NQ * BM), a.nHead, a.nseq);
+    kern<<<grid, S_::THREADS, smem, s>>>(qm, km, vm, p);
     return cudaGetLastError();
+}
+
+}  // namespace
+
+#ifndef TL_PREFILL_NQ
+#define TL_PREFILL_NQ 2
+#endif
+
+cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s) {
+    if (a.headDim != HD || a.kv.dtype != TL_KV_BF16 || a.qb == nullptr || a.pos0 != nullptr ||
+        a.kf.ptr != nullptr)
+        return cudaErrorNotSupported;
+#if TL_PREFILL_NQ == 3
+    return launch_shape<3, 64>(a, s);
+#else
+    return launch_shape<2, 128>(a, s);
+#endif
 }
 
 }  // namespace tl
