@@ -172,9 +172,9 @@ TL_API int tl_check_device(tl_attn *h, void *stream);
 /* ---- allocation-free decode ------------------------------------------------------------- */
 
 /* No counterpart in the reference.  For callers that cannot allocate device memory (a host
- * whose allocator owns all of it, code running under CUDA graph capture, a loop that must not
- * take an allocation's latency): the same split-KV decode attention as tl_decode_attention,
- * without a handle and without any allocation.  The caller passes q [nseq][nHead*headDim],
+ * whose allocator has reserved all of it up front, or a loop that must not take an
+ * allocation's latency and implicit synchronisation): the same split-KV decode attention as
+ * tl_decode_attention, without a handle and without any allocation.  The caller passes q [nseq][nHead*headDim],
  * the cache K and V, each head-major [nseq][nHeadKv][maxLen][headDim] of f32 or bf16 with
  * RoPE already applied, positions pos_dev / pos_host (both required; sequence b attends
  * positions 0..pos[b]) and out [nseq][nHead*headDim], all on the current device; the call is

@@ -2,7 +2,7 @@
 one (tl_decode_attention), through the C ABI, on a B200.
 
 It exists for callers that cannot call cudaMalloc -- a host whose allocator owns all device
-memory, code under CUDA graph capture, a loop that must not pay an allocation's latency -- and
+memory, a loop that must not pay an allocation's latency -- and
 keeps its scratch in a fixed array inside the library.  Two calls in a row must both match the
 handle-based result, which shows the shared scratch is cleared between calls.  This file is
 collected last so that a stop-at-first-failure run has run every other test before it."""

@@ -1,9 +1,9 @@
 // decode_noalloc.cu -- decode attention that allocates nothing.
 //
 // Some callers cannot call cudaMalloc: a host whose allocator owns all device memory (a
-// serving engine that carves one pre-reserved pool and forbids other allocations), code
-// running while a CUDA graph is being captured or replayed, or a real-time loop in which an
-// allocation's latency and possible implicit synchronisation are not allowed.  For them
+// serving engine that carves one pre-reserved pool and forbids other allocations), or a
+// real-time loop in which an allocation's latency and possible implicit synchronisation are
+// not allowed.  For them
 // tl_decode_attention_noalloc runs the same split-KV decode kernel as tl_decode_attention,
 // but without a tl_attn handle: the caller passes q, the K/V cache and the output, and the
 // kernel's scratch -- chunk partials, arrival counters and the device error word -- lives in
