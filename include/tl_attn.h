@@ -189,19 +189,28 @@ TL_API int tl_decode_attention_noalloc(const float *q, const void *k_cache, cons
                                        int nseq, const int *pos_dev, const int *pos_host, float *out,
                                        void *stream);
 
-/* ---- multi-GPU split-KV (one process per GPU, NCCL over NVLink) ---------------------------- */
+/* ---- multi-GPU split-KV (one process per GPU, peer memory over NVLink) --------------------- */
 
 /* NCCL unique id (128 bytes) created on one rank and shared with the others by the caller. */
 TL_API int tl_dist_unique_id(char *id128);
-/* Join the communicator: rank `rank` of `nranks`, this handle's device.  The handle's cache
- * then holds positions [rank*maxLen, (rank+1)*maxLen) of every sequence (its slice). */
+/* Collective.  Join the group as rank `rank` of `nranks` (at most 8, one process per GPU on
+ * one NVSwitch domain), on this handle's device.  The handle's cache then holds positions
+ * [rank*maxLen, (rank+1)*maxLen) of every sequence (its slice).  Every rank exports an exchange
+ * buffer with CUDA IPC and maps every peer's; NCCL is used here only to pass the IPC handles.
+ * If the peers cannot be mapped (or TL_DIST_NCCL=1 is set), the calls below exchange through
+ * an NCCL all-gather instead. */
 TL_API int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank);
-/* Split-KV decode across the ranks: every rank passes the same q [nseq][nHead*headDim]
- * (already rotated) and global positions pos_dev/pos_host (the query attends global positions
- * 0..pos[b]); each rank attends its slice, the (m, l, o) partials are all-gathered with NCCL
- * and merged, and every rank receives the full out [nseq][nHead*headDim]. */
+/* Collective: every rank makes the same sequence of calls.  Split-KV decode across the ranks:
+ * every rank passes the same q [nseq][nHead*headDim] (already rotated) and global positions
+ * pos_dev/pos_host (the query attends global positions 0..pos[b]); each rank attends its
+ * slice, the kernel stores each (sequence, head)'s (o, m, l) into every rank's buffer over
+ * NVLink and merges them, and every rank receives the full out [nseq][nHead*headDim].  One
+ * kernel launch per call on `stream`; its waits for the peers are bounded (2 s), after which
+ * the device error word reports a timeout (tl_check_device). */
 TL_API int tl_decode_attention_dist(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
                              const int *pos_host, const float *q, float *out, void *stream);
+/* Collective: synchronises the device, waits for every rank, unmaps the peers' buffers and
+ * leaves the group (tl_attn_destroy does this too). */
 TL_API void tl_dist_finalize(tl_attn *h);
 
 #ifdef __cplusplus

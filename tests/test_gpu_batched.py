@@ -3,6 +3,7 @@ configurations of the batched decode (independent sequences of ragged length, 32
 heads, head_dim 128), long-context split-KV (32 q / 8 kv heads, theta 5e5) and the batched
 prefill (32 q / 8 kv heads, head_dim 64), at sizes the oracle finishes in seconds."""
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -180,28 +181,39 @@ def test_prefill_step_batched(env, kvd, S):
         _lib.lib.tl_attn_destroy(h)
 
 
-def test_dist_single_rank_matches_local(env):
-    """tl_decode_attention_dist with one rank: the (m, l, o) partial path, the NCCL all-gather
-    and the merge kernel must reproduce the single-GPU result."""
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_dist_single_rank_matches_local(env, exchange):
+    """tl_decode_attention_dist with one rank must reproduce the single-GPU result.  "peer" is
+    the fused exchange (the decode kernel stores its (o, m, l) into the gather buffer, raises
+    the epoch flag, waits for it and merges); "nccl" is the fallback (local partials, NCCL
+    all-gather, merge launch), chosen by TL_DIST_NCCL=1 at tl_dist_init.  Three calls in a row
+    use both halves of the exchange buffer."""
     torch, _lib = env
     rng = np.random.default_rng(31)
     lens = [3000, 129, 1]
     B, Hq, Hkv, D = 3, 32, 8, 128
+    old = os.environ.pop("TL_DIST_NCCL", None)
+    if exchange == "nccl":
+        os.environ["TL_DIST_NCCL"] = "1"
     h = create(_lib, 1, Hq, Hkv, D, 4096, B, 1, 500000.0)
     try:
         fill_cache(torch, _lib, h, 0, lens, Hkv, D, rng, 500000.0, 1)
         uid = C.create_string_buffer(128)
         _lib.check(_lib.lib.tl_dist_unique_id(uid))
         _lib.check(_lib.lib.tl_dist_init(h, uid, 1, 0))
-        q = torch.from_numpy(randn(rng, B, Hq * D)).cuda()
         pos = np.array([L - 1 for L in lens], np.int32)
         dpos = torch.from_numpy(pos).cuda()
-        o1 = torch.empty(B, Hq * D, device="cuda")
-        o2 = torch.empty(B, Hq * D, device="cuda")
         f = pos.ctypes.data_as(C.c_void_p)
-        _lib.check(_lib.lib.tl_decode_attention(h, 0, 0, B, ptr(dpos), f, ptr(q), ptr(o1), None))
-        _lib.check(_lib.lib.tl_decode_attention_dist(h, 0, 0, B, ptr(dpos), f, ptr(q), ptr(o2), None))
-        _lib.check(_lib.lib.tl_check_device(h, None))
-        assert torch.allclose(o1, o2, rtol=1e-4, atol=1e-5)
+        for _ in range(3):
+            q = torch.from_numpy(randn(rng, B, Hq * D)).cuda()
+            o1 = torch.empty(B, Hq * D, device="cuda")
+            o2 = torch.empty(B, Hq * D, device="cuda")
+            _lib.check(_lib.lib.tl_decode_attention(h, 0, 0, B, ptr(dpos), f, ptr(q), ptr(o1), None))
+            _lib.check(_lib.lib.tl_decode_attention_dist(h, 0, 0, B, ptr(dpos), f, ptr(q), ptr(o2), None))
+            _lib.check(_lib.lib.tl_check_device(h, None))
+            assert torch.allclose(o1, o2, rtol=1e-4, atol=1e-5)
     finally:
         _lib.lib.tl_attn_destroy(h)
+        os.environ.pop("TL_DIST_NCCL", None)
+        if old is not None:
+            os.environ["TL_DIST_NCCL"] = old

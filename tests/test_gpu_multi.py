@@ -1,6 +1,9 @@
-"""Split-KV decode across two GPUs (tl_decode_attention_dist over NCCL) against the single-GPU
-decode over the whole context, on two B200s.  One process per GPU, spawned; the NCCL id is
-created in the parent and passed to both."""
+"""Split-KV decode across two GPUs (tl_decode_attention_dist: the decode kernel stores each
+(sequence, head) result into every rank's buffer over NVLink and merges after a bounded flag
+wait) against the single-GPU decode over the whole context, on two B200s.  One process per GPU,
+spawned; the NCCL id (used once, to exchange the IPC handles) is created in the parent.  Three
+calls in a row with different queries exercise both halves of the double-buffered exchange and
+the epoch flags."""
 import ctypes as C
 import multiprocessing as mp
 import os
@@ -28,7 +31,7 @@ def _worker(rank, nranks, uid, kvd, L, out_q):
     rng = np.random.default_rng(7 + kvd)
     k = rng.standard_normal((B, L, Hkv * D), dtype=np.float32)
     v = rng.standard_normal((B, L, Hkv * D), dtype=np.float32)
-    q = rng.standard_normal((B, Hq * D), dtype=np.float32)
+    qs = [rng.standard_normal((B, Hq * D), dtype=np.float32) for _ in range(3)]
     lens = [L - 1, L // 2 - 3]  # the second sequence ends inside rank 0's slice
     p = lambda t: C.c_void_p(t.data_ptr())
     h = C.c_void_p()
@@ -41,12 +44,13 @@ def _worker(rank, nranks, uid, kvd, L, out_q):
         _lib.check(_lib.lib.tl_dist_init(h, C.create_string_buffer(uid, 128), nranks, rank))
         pos = np.array(lens, np.int32)
         dpos = torch.from_numpy(pos).cuda()
-        dq = torch.from_numpy(q).cuda()
-        out = torch.empty(B, Hq * D, device="cuda")
-        _lib.check(_lib.lib.tl_decode_attention_dist(h, 0, 0, B, p(dpos), pos.ctypes.data_as(C.c_void_p),
-                                                     p(dq), p(out), None))
+        dqs = [torch.from_numpy(q).cuda() for q in qs]
+        outs = [torch.empty(B, Hq * D, device="cuda") for _ in qs]
+        for dq, out in zip(dqs, outs):  # back to back, no host synchronisation in between
+            _lib.check(_lib.lib.tl_decode_attention_dist(h, 0, 0, B, p(dpos), pos.ctypes.data_as(C.c_void_p),
+                                                         p(dq), p(out), None))
         _lib.check(_lib.lib.tl_check_device(h, None))
-        got = out.cpu().numpy()
+        got = [out.cpu().numpy() for out in outs]
         ref = None
         if rank == 0:  # whole context on one GPU
             h1 = C.c_void_p()
@@ -55,11 +59,13 @@ def _worker(rank, nranks, uid, kvd, L, out_q):
                 kk = torch.from_numpy(np.ascontiguousarray(k[b])).cuda()
                 vv = torch.from_numpy(np.ascontiguousarray(v[b])).cuda()
                 _lib.check(_lib.lib.tl_kv_store(h1, 0, b, 0, p(kk), p(vv), L, None))
-            o1 = torch.empty(B, Hq * D, device="cuda")
-            _lib.check(_lib.lib.tl_decode_attention(h1, 0, 0, B, p(dpos), pos.ctypes.data_as(C.c_void_p),
-                                                    p(dq), p(o1), None))
-            _lib.check(_lib.lib.tl_check_device(h1, None))
-            ref = o1.cpu().numpy()
+            ref = []
+            for dq in dqs:
+                o1 = torch.empty(B, Hq * D, device="cuda")
+                _lib.check(_lib.lib.tl_decode_attention(h1, 0, 0, B, p(dpos), pos.ctypes.data_as(C.c_void_p),
+                                                        p(dq), p(o1), None))
+                _lib.check(_lib.lib.tl_check_device(h1, None))
+                ref.append(o1.cpu().numpy())
             _lib.lib.tl_attn_destroy(h1)
         out_q.put((rank, got, ref, None))
     except Exception as e:  # report, never hang the parent
@@ -93,7 +99,7 @@ def test_splitkv_two_gpus_matches_one(cuda_lib, kvd):
             pr.join(timeout=60)
             if pr.is_alive():
                 pr.kill()
-    ref = results[0][1]
+    refs = results[0][1]
     for rank in (0, 1):
-        got = results[rank][0]
-        assert np.allclose(got, ref, rtol=1e-4, atol=1e-5), (rank, float(np.max(np.abs(got - ref))))
+        for i, (got, ref) in enumerate(zip(results[rank][0], refs)):
+            assert np.allclose(got, ref, rtol=1e-4, atol=1e-5), (rank, i, float(np.max(np.abs(got - ref))))

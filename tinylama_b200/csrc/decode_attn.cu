@@ -304,6 +304,8 @@ decode_kernel(const DecodeArgs a) {
         // shared scratch is reused by the next unit; leave together if any warp aborted
         if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
     }
+    // split-KV across GPUs: this CTA's share of the cross-rank merges, after its own units
+    if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);
 }
 
 // Merge G per-rank (o, m, l) partials into the final context.

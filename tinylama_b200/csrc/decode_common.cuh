@@ -34,8 +34,9 @@ __device__ __forceinline__ int local_len(const DecodeArgs &a, int b, unsigned *e
     const int pos = a.pos[b];
     const int slice = a.kv.maxLen;
     if (pos < 0 || pos - a.pos_offset >= slice) {
-        // single-GPU: the appended token must sit inside the cache
-        if (a.lse_out == nullptr || pos < 0) atomicOr(err, TL_DEVERR_POS_RANGE);
+        // single-GPU: the appended token must sit inside the cache (a split-KV shard only
+        // covers part of the positions)
+        if ((a.lse_out == nullptr && a.px.nranks == 0) || pos < 0) atomicOr(err, TL_DEVERR_POS_RANGE);
     }
     int n = pos + 1 - a.pos_offset;
     n = n < 0 ? 0 : (n > slice ? slice : n);
@@ -94,6 +95,92 @@ __device__ __forceinline__ void build_schedule(const DecodeArgs &a, int *prefix,
         if (lane == 31) prefix[a.nseq] = incl;
     }
 
+// ---- split-KV across GPUs over peer memory ------------------------------------------------
+// Exchange words: the float's bits in the low half, the call's epoch in the high half.
+__device__ __forceinline__ void st_word_sys(unsigned long long *p, float v, unsigned epoch) {
+    const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Wait (bounded by TL_WAIT_NS from t0) until the word carries this call's epoch; epochs only
+// grow.  Returns the value, or 0 with *ok cleared (and the timeout bit set) on time-out.
+__device__ __forceinline__ float wait_word(const unsigned long long *p, unsigned epoch, uint64_t t0, bool *ok,
+                                           unsigned *err) {
+    unsigned long long w = ld_word_sys(p);
+    while ((int)((unsigned)(w >> 32) - epoch) < 0) {
+        if (!*ok) return 0.f;
+        if (globaltimer_ns() - t0 > TL_WAIT_NS) {
+            atomicOr(err, TL_DEVERR_TIMEOUT);
+            *ok = false;
+            return 0.f;
+        }
+        w = ld_word_sys(p);
+    }
+    return __uint_as_float((unsigned)w);
+}
+
+// The final (o, m, l) of (sequence b, head) into slot `rank` of every rank's gather buffer
+// (peer stores over NVLink; the own rank's entry is local memory).
+template <int D>
+__device__ __forceinline__ void peer_store_final(const DecodeArgs &a, int b, int head, int dd, float O, float M,
+                                                 float L) {
+    const int64_t row = (int64_t)a.px.rank * a.nseq * a.nHead + (int64_t)b * a.nHead + head;
+    for (int r = 0; r < a.px.nranks; ++r) {
+        unsigned long long *dst = a.px.gather[r] + row * (D + 2);
+        st_word_sys(dst + dd, O, a.px.epoch);
+        if (dd == 0) {
+            st_word_sys(dst + D, M, a.px.epoch);
+            st_word_sys(dst + D + 1, L, a.px.epoch);
+        }
+    }
+}
+
+// After its own units, CTA i merges the pairs p = i, i + gridDim, ... of this call, reading the
+// ranks' words of p's G heads as they arrive:
+//   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L.
+// A CTA waits only once its own units are done, and no rank's units wait on anything, so the
+// waits cannot form a cycle.  Called by the NW*32 consumer threads.
+template <int G, int D, int NW>
+__device__ __forceinline__ void peer_merge_pairs(const DecodeArgs &a, int tid) {
+    const int R = a.px.nranks;
+    const int pairs = a.nseq * a.nHeadKv;
+    const unsigned long long *g = a.px.gather[a.px.rank];
+    const int64_t stride = (int64_t)a.nseq * a.nHead * (D + 2);
+    const uint64_t t0 = globaltimer_ns();
+    bool ok = true;
+    for (int p = blockIdx.x; p < pairs && ok; p += gridDim.x) {
+        const int b = p / a.nHeadKv, grp = p - b * a.nHeadKv;
+        for (int e = tid; e < G * D && ok; e += NW * 32) {
+            const int h = e / D, dd = e - h * D;
+            const int64_t row = (int64_t)b * a.nHead + grp * G + h;
+            const unsigned long long *pr = g + row * (D + 2);
+            float m[kMaxPeers], l[kMaxPeers], o[kMaxPeers];
+            float M = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+                if (r >= R) break;
+                m[r] = wait_word(pr + r * stride + D, a.px.epoch, t0, &ok, a.err);
+                l[r] = wait_word(pr + r * stride + D + 1, a.px.epoch, t0, &ok, a.err);
+                o[r] = wait_word(pr + r * stride + dd, a.px.epoch, t0, &ok, a.err);
+                M = fmaxf(M, m[r]);
+            }
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+                if (r >= R) break;
+                const float w = safe_exp2_diff(m[r], M);
+                L = fmaf(l[r], w, L);
+                O = fmaf(o[r], w, O);
+            }
+            if (ok) a.out[row * D + dd] = (L > 0.f) ? O / L : 0.f;
+        }
+    }
+}
+
 // Merge of the NW consumer warps' states (written to wm[NW][G], wl[NW][G], wo[NW][G][D]) at the
 // end of unit u, then the cross-chunk merge by the last CTA.  Called by the NW*32 consumer
 // threads of the CTA; uses named barrier 1.
@@ -102,7 +189,8 @@ __device__ __forceinline__ void unit_epilogue(const DecodeArgs &a, const Unit &u
                                               float *wm, float *wl, float *wo, float *cw, int *is_last_flag,
                                               int tid, int warp, int lane) {
         named_bar(1, NW * 32);
-        const bool single = (un.nch == 1) && (a.lse_out == nullptr);
+        const bool peer = a.px.nranks > 0;
+        const bool single = (un.nch == 1) && (a.lse_out == nullptr) && !peer;
         const int unit_index = u;  // partial slot of this unit
         for (int e = tid; e < G * D; e += NW * 32) {
             const int h = e / D, dd = e - h * D;
@@ -119,6 +207,8 @@ __device__ __forceinline__ void unit_epilogue(const DecodeArgs &a, const Unit &u
             const int head = un.g * G + h;
             if (single) {
                 a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
+            } else if (un.nch == 1 && peer) {
+                peer_store_final<D>(a, un.b, head, dd, O, M, L);
             } else if (un.nch == 1) {
                 float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);
                 dst[dd] = O;
@@ -182,7 +272,9 @@ __device__ __forceinline__ void unit_epilogue(const DecodeArgs &a, const Unit &u
                     O = (O + O1) + (O2 + O3);
                     const int head = un.g * G + h;
                     const float L = wl[h];
-                    if (a.lse_out == nullptr) {
+                    if (peer) {
+                        peer_store_final<D>(a, un.b, head, dd, O, wm[h], L);
+                    } else if (a.lse_out == nullptr) {
                         a.out[((int64_t)un.b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
                     } else {
                         float *dst = a.lse_out + ((int64_t)un.b * a.nHead + head) * (D + 2);

@@ -299,6 +299,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
         unit_epilogue<G, D, C::NW>(a, un, u, prefix, wm, wl, wo, cw, is_last_flag, tid, warp, lane);
         if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
     }
+    // split-KV across GPUs: this CTA's share of the cross-rank merges, after its own units
+    if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {

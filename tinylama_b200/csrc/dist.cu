@@ -1,18 +1,36 @@
-// dist.cu -- split-KV decode across GPUs: one process per GPU, NCCL over NVLink/NVSwitch.
+// dist.cu -- split-KV decode across GPUs: one process per GPU on one NVSwitch domain.
 //
 // The reference has no parallelism on this path (attentionCached, src/forward.nim:179-211,
 // is one CPU loop).  Long contexts are split along the sequence axis: rank r's cache holds
 // global positions [r*maxLen, (r+1)*maxLen) of every sequence.  Each rank runs the split-KV
-// decode kernel over its slice and writes per-(sequence, q-head) partials (o, m, l) -- m and l
-// in the log2 domain -- into its own slot of a gather buffer; one in-place ncclAllGather
-// exchanges the slots (B*nHead*(headDim+2) floats per rank) and a merge kernel combines them:
+// decode kernel over its slice; the per-(sequence, q-head) results (o, m, l) -- m and l in the
+// log2 domain -- are combined as
 //   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L.
+//
+// The exchange is fused into the decode kernel over peer memory.  At tl_dist_init every rank
+// exports one buffer with CUDA IPC (two halves of [nranks][maxBatch*nHead][headDim+2] 8-byte
+// words), the handles are all-gathered once over NCCL, and every rank maps every peer's
+// buffer.  In a call, the CTA that finishes a (sequence, kv-head) stores its heads' (o, m, l)
+// straight into slot `rank` of every rank's buffer (NVLink stores) as words that carry the
+// value and the call's epoch; after its own units each CTA merges a share of the pairs, reading
+// each word once it shows the current epoch (a bounded wait).  An aligned 8-byte store is
+// single-copy atomic, so the epoch in a word vouches for its value: no fences, no flags, one
+// launch per call and no collective.  Calls alternate between the two halves by epoch parity,
+// so a rank that runs ahead into the next call never overwrites words a slower rank has not
+// read yet.
+//
+// If the peers cannot be mapped (ranks in one process, or TL_DIST_NCCL=1 in the environment at
+// tl_dist_init), the exchange falls back to writing the local slot, one in-place
+// ncclAllGather and a merge launch.
 #include <dlfcn.h>
 #include <nccl.h>
 #include <string.h>
 
+#include <stdlib.h>
+
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "internal.h"
 
@@ -20,6 +38,9 @@ namespace tl {
 int api_run_decode_lse(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
                        const int *pos_host, const float *q, float *lse_out, cudaStream_t s,
                        int pos_offset);
+int api_run_decode_peer(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
+                        const int *pos_host, const float *q, float *out, cudaStream_t s, int pos_offset,
+                        const DecodeArgs::Peer &px);
 int api_fail(int code, const char *msg);
 }  // namespace tl
 
@@ -68,6 +89,96 @@ int nccl_fail(ncclResult_t r, const char *what) {
         if (!nccl().ok) return api_fail(TL_ERR_NCCL, "libnccl.so.2 could not be loaded"); \
     } while (0)
 
+// All ranks reach this point: an all-gather of one float per rank on the handle's stream.
+int dist_barrier(tl_attn *h) {
+    float *d = nullptr;
+    if (cudaMalloc(&d, sizeof(float) * h->nranks) != cudaSuccess) return api_fail(TL_ERR_NOMEM, "barrier buffer");
+    ncclResult_t r = nccl().AllGather(d + h->rank, d, 1, ncclFloat, reinterpret_cast<ncclComm_t>(h->comm), h->stream);
+    cudaStreamSynchronize(h->stream);
+    cudaFree(d);
+    return r == ncclSuccess ? TL_OK : nccl_fail(r, "ncclAllGather (barrier)");
+}
+
+void unmap_peers(tl_attn *h) {
+    for (int r = 0; r < h->nranks && r < kMaxPeers; ++r) {
+        if (r != h->rank && h->peerBase[r]) cudaIpcCloseMemHandle(h->peerBase[r]);
+        h->peerBase[r] = nullptr;
+    }
+}
+
+// Collective: export this rank's exchange buffer, all-gather the IPC handles, map the peers'.
+// Returns TL_OK with peerBase[rank] == nullptr when the peers cannot be mapped (the NCCL
+// exchange is used then).
+int map_peers(tl_attn *h) {
+    const char *env = getenv("TL_DIST_NCCL");
+    const bool want = h->nranks <= kMaxPeers && !(env && env[0] == '1');
+    const size_t half = (size_t)h->nranks * h->maxBatch * h->nHead * (h->headDim + 2);
+    const size_t bytes = 2 * half * sizeof(unsigned long long);
+    if (want) {
+        if (cudaMalloc(&h->dPeerBuf, bytes) != cudaSuccess)
+            return api_fail(TL_ERR_NOMEM, "split-KV exchange buffer allocation failed");
+        cudaMemset(h->dPeerBuf, 0, bytes);  // every word starts at epoch 0
+        h->peerHalfWords = half;
+    }
+    // every rank takes part in the handle exchange, also one that does not map (all-or-nothing)
+    cudaIpcMemHandle_t mine{};
+    int ok = want && (h->nranks == 1 || cudaIpcGetMemHandle(&mine, h->dPeerBuf) == cudaSuccess);
+    const size_t rec = sizeof(cudaIpcMemHandle_t) + 8;
+    std::vector<char> host(rec * h->nranks);
+    char *dev = nullptr;
+    if (cudaMalloc(&dev, rec * h->nranks) != cudaSuccess) return api_fail(TL_ERR_NOMEM, "handle exchange buffer");
+    std::vector<char> me(rec, 0);
+    memcpy(me.data(), &mine, sizeof mine);
+    memcpy(me.data() + sizeof mine, &ok, sizeof ok);
+    cudaMemcpy(dev + rec * h->rank, me.data(), rec, cudaMemcpyHostToDevice);
+    cudaDeviceSynchronize();  // the zeroed words are in place before any peer can map them
+    ncclResult_t r = nccl().AllGather(dev + rec * h->rank, dev, rec, ncclChar, reinterpret_cast<ncclComm_t>(h->comm),
+                                      h->stream);
+    cudaStreamSynchronize(h->stream);
+    cudaMemcpy(host.data(), dev, rec * h->nranks, cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather (IPC handles)");
+    int all_ok = 1;
+    for (int q = 0; q < h->nranks; ++q) {
+        int o = 0;
+        memcpy(&o, host.data() + rec * q + sizeof(cudaIpcMemHandle_t), sizeof o);
+        all_ok &= o;
+    }
+    if (all_ok) {
+        for (int q = 0; q < h->nranks; ++q) {
+            if (q == h->rank) { h->peerBase[q] = h->dPeerBuf; continue; }
+            cudaIpcMemHandle_t hq;
+            memcpy(&hq, host.data() + rec * q, sizeof hq);
+            if (cudaIpcOpenMemHandle(&h->peerBase[q], hq, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                h->peerBase[q] = nullptr;
+                all_ok = 0;
+            }
+        }
+    }
+    // agree on the outcome: the fused exchange runs only if every rank mapped every peer
+    int agreed = all_ok;
+    {
+        std::vector<char> again(rec, 0);
+        memcpy(again.data() + sizeof(cudaIpcMemHandle_t), &all_ok, sizeof all_ok);
+        char *d2 = nullptr;
+        if (cudaMalloc(&d2, rec * h->nranks) != cudaSuccess) return api_fail(TL_ERR_NOMEM, "handle exchange buffer");
+        cudaMemcpy(d2 + rec * h->rank, again.data(), rec, cudaMemcpyHostToDevice);
+        r = nccl().AllGather(d2 + rec * h->rank, d2, rec, ncclChar, reinterpret_cast<ncclComm_t>(h->comm), h->stream);
+        cudaStreamSynchronize(h->stream);
+        cudaMemcpy(host.data(), d2, rec * h->nranks, cudaMemcpyDeviceToHost);
+        cudaFree(d2);
+        if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather (IPC outcome)");
+        for (int q = 0; q < h->nranks; ++q) {
+            int o = 0;
+            memcpy(&o, host.data() + rec * q + sizeof(cudaIpcMemHandle_t), sizeof o);
+            agreed &= o;
+        }
+    }
+    if (!agreed) unmap_peers(h);
+    return TL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -100,7 +211,10 @@ int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank) {
     h->comm = comm;
     h->nranks = nranks;
     h->rank = rank;
-    return TL_OK;
+    cudaSetDevice(h->device);
+    const int rc = map_peers(h);
+    cudaSetDevice(prev);
+    return rc;
 }
 
 void tl_dist_finalize(tl_attn *h) {
@@ -108,7 +222,18 @@ void tl_dist_finalize(tl_attn *h) {
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
-    if (h->stream) cudaStreamSynchronize(h->stream);
+    cudaDeviceSynchronize();
+    if (h->dPeerBuf) {
+        // every rank's kernels are done before any mapping goes, and every mapping is gone
+        // before any exporter frees its buffer
+        dist_barrier(h);
+        unmap_peers(h);
+        dist_barrier(h);
+        cudaFree(h->dPeerBuf);
+        h->dPeerBuf = nullptr;
+        h->peerHalfWords = 0;
+        h->epoch = 0;
+    }
     nccl().CommDestroy(reinterpret_cast<ncclComm_t>(h->comm));
     cudaSetDevice(prev);
     h->comm = nullptr;
@@ -130,6 +255,18 @@ int tl_decode_attention_dist(tl_attn *h, int layer, int slot0, int nseq, const i
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : h->stream;
+    if (h->peerBase[h->rank]) {
+        DecodeArgs::Peer px{};
+        px.epoch = ++h->epoch;
+        const size_t half = (px.epoch & 1u) ? h->peerHalfWords : 0;
+        for (int r = 0; r < h->nranks; ++r) px.gather[r] = reinterpret_cast<unsigned long long *>(h->peerBase[r]) + half;
+        px.nranks = h->nranks;
+        px.rank = h->rank;
+        const int rc = api_run_decode_peer(h, layer, slot0, nseq, pos_dev, pos_host, q, out, s,
+                                           h->rank * h->maxLen, px);
+        cudaSetDevice(prev);
+        return rc;
+    }
     const size_t rows = (size_t)nseq * h->nHead;
     const size_t per_rank = rows * (h->headDim + 2);
     const size_t need = per_rank * h->nranks;

@@ -13,6 +13,7 @@
 namespace tl {
 
 constexpr int kMaxRopePairs = 128;  // headDim <= 256
+constexpr int kMaxPeers = 8;        // GPUs in a split-KV group (one NVSwitch domain of an HGX node)
 
 // RoPE frequencies, computed on the host with the same float32 powf as src/forward.nim:116
 // (theta_i = powf(1/base, 2i/ropeDim)) and passed by value to the kernels, so device and
@@ -74,10 +75,16 @@ struct tl_attn {
     size_t qbCap = 0;               // bytes
     cudaStream_t stream = nullptr;  // the handle's own stream (host tier)
     // multi-GPU split-KV
-    void *comm = nullptr;           // ncclComm_t
+    void *comm = nullptr;           // ncclComm_t (used to exchange the IPC handles)
     int nranks = 1, rank = 0;
     float *dGather = nullptr;
     size_t gatherCap = 0;
+    // peer-memory exchange: this rank's exported buffer ([2 halves][nranks][maxBatch*nHead]
+    // [headDim+2] 8-byte words) and every rank's mapping of it
+    void *dPeerBuf = nullptr;
+    void *peerBase[tl::kMaxPeers] = {};
+    size_t peerHalfWords = 0;
+    unsigned epoch = 0;
 };
 
 namespace tl {
@@ -121,6 +128,17 @@ struct DecodeArgs {
     // When non-null the kernel writes un-normalised (m, l, o) per (seq, head) here instead
     // of the final output: [nseq][nHead][headDim + 2] = (o[0..d), m, l).
     float *lse_out;
+    // Split-KV across GPUs over peer memory (dist.cu); inactive when nranks == 0.  The CTA that
+    // finishes a (sequence, kv-head) pair stores its heads' (o, m, l) into slot `rank` of every
+    // rank's gather buffer as 8-byte words (float bits, epoch): a word is single-copy atomic,
+    // so a reader that sees the current epoch in a word also sees its value, and no fence or
+    // flag is needed.  After its own units, CTA i merges the pairs p = i, i + gridDim, ...,
+    // waiting (bounded) on each word it reads.
+    struct Peer {
+        unsigned long long *gather[kMaxPeers];  // rank r's half for this call: [nranks][nseq*nHead][D+2]
+        unsigned epoch;
+        int nranks, rank;
+    } px;
 };
 cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s);
 int decode_ctas_per_sm(int headDim, int group, int dtype);

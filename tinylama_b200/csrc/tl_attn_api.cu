@@ -180,7 +180,8 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
 }
 
 int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, const int *pos_host,
-               const float *q, float *out, cudaStream_t s, int pos_offset, float *lse_out) {
+               const float *q, float *out, cudaStream_t s, int pos_offset, float *lse_out,
+               const DecodeArgs::Peer *px = nullptr) {
     Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen);
     TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
     DecodeArgs a{};
@@ -201,6 +202,7 @@ int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, c
     a.counter = h->dCounter + (size_t)slot0 * h->nHeadKv;
     a.err = h->dErr;
     a.lse_out = lse_out;
+    if (px) a.px = *px;
     cudaError_t e = launch_decode(a, p.ctas, s);
     if (e == cudaErrorNotSupported) return fail(TL_ERR_UNSUPPORTED, "decode: shape not covered");
     TL_CUDA(e);
@@ -786,6 +788,12 @@ int api_run_decode_lse(tl_attn *h, int layer, int slot0, int nseq, const int *po
                        const int *pos_host, const float *q, float *lse_out, cudaStream_t s,
                        int pos_offset) {
     return run_decode(h, layer, slot0, nseq, pos_dev, pos_host, q, nullptr, s, pos_offset, lse_out);
+}
+
+int api_run_decode_peer(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
+                        const int *pos_host, const float *q, float *out, cudaStream_t s, int pos_offset,
+                        const DecodeArgs::Peer &px) {
+    return run_decode(h, layer, slot0, nseq, pos_dev, pos_host, q, out, s, pos_offset, nullptr, &px);
 }
 int api_fail(int code, const char *msg) { return fail(code, "%s", msg); }
 }  // namespace tl
