@@ -153,7 +153,8 @@ def seq_lens(seed: int, n: int, lo: int = 256, hi: int = 4096) -> np.ndarray:
 
 # ------------------------------------------------------------------- decode (batched) arm
 class DecodeBatched:
-    """256 sequences, 32/32 heads, head_dim 128, L ~ U[256, 4096], f32 (or bf16) KV."""
+    """256 sequences, L ~ U[256, 4096], f32 (or bf16) KV; 32/32 heads of head_dim 128 (Llama-2-7B
+    style) by default, or the TinyLlama GQA shape 32/4 heads of head_dim 64."""
 
     def __init__(self, kvd: int, rank: int, B=256, Hq=32, Hkv=32, D=128, base=10000.0):
         import torch
@@ -307,10 +308,12 @@ def cpu_decode_sample(lens, Hq, Hkv, D, base, budget_s: float, threads: int, see
 
 
 # ------------------------------------------------------------------------------ workloads
-def run_decode_batched(args, dist, kvd: int):
+def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
     import torch
     pk = peaks()
-    w = DecodeBatched(kvd, dist.rank, B=args.seqs)
+    Hq, Hkv, D = shape
+    gqa = Hkv != Hq
+    w = DecodeBatched(kvd, dist.rank, B=args.seqs, Hq=Hq, Hkv=Hkv, D=D)
     sampler = ClockSampler(dist.local)
     sampler.start()
     ms = time_steps(w.step, args.steps, args.warmup, w.stream, dist)
@@ -321,12 +324,13 @@ def run_decode_batched(args, dist, kvd: int):
     achieved = w.algorithmic_bytes_attention() / (ms_attn / 1e3) / 1e9
     e2e_dt, h2d, d2h = w.e2e(max(3, args.steps // 4), 2, dist)
     e2e_value = n * w.B / e2e_dt
-    traffic = traffic_from_profiles("decode_kernel_f32" if kvd == 0 else "decode_kernel_bf16")
+    traffic = traffic_from_profiles(("decode_kernel_f32" if kvd == 0 else "decode_kernel_bf16") + ("_gqa" if gqa else ""))
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": n, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32" if kvd == 0 else "bf16-kv/f32-math", "data": "synthetic",
-        "config": {"workload": "batched multi-sequence decode (Llama-2-7B-style attention)",
+        "config": {"workload": "batched multi-sequence decode (TinyLlama GQA attention)" if gqa else
+                               "batched multi-sequence decode (Llama-2-7B-style attention)",
                    "seqs_per_gpu": w.B, "global_batch": w.B * n, "ctx_len": "U[256,4096] seeded",
                    "mean_ctx": float(np.mean(w.lens)), "n_head": w.Hq, "n_head_kv": w.Hkv,
                    "head_dim": w.D, "kv_dtype": "f32" if kvd == 0 else "bf16",
@@ -343,10 +347,10 @@ def run_decode_batched(args, dist, kvd: int):
                      "algorithmic_bytes_per_launch": w.algorithmic_bytes_attention(),
                      "launch_ms": round(ms_attn, 4)},
     }
-    if not args.no_prefill:
+    if not args.no_prefill and not gqa:
         res["prefill"] = run_prefill(args, dist)
         res["decode_tinyllama"] = run_decode_tiny(args, dist)
-    if n == 1 and dist.rank == 0 and not args.no_cpu_baseline:
+    if n == 1 and dist.rank == 0 and not args.no_cpu_baseline and not gqa:
         rate, sample = cpu_decode_sample(w.lens, w.Hq, w.Hkv, w.D, w.base, args.cpu_budget, 1)
         res["cpu_baseline"] = {"value": round(rate, 3), "unit": "tok/s", "cores": 1, "kind": "port",
                                "sample": sample + "; Malebolgia on/off identical (attention has no "
@@ -356,35 +360,59 @@ def run_decode_batched(args, dist, kvd: int):
 
 
 # -------------------------------------------------------------------- prefill (tcgen05)
-def prefill_point(S: int, steps: int, warmup: int, B=8, Hq=32, Hkv=8, D=64, kvd=1):
-    """Causal prefill of B sequences of S tokens: RoPE + bf16 cache write + attention
-    (tl_prefill_step).  Returns (ms per step, TFLOP/s of the attention, flops)."""
+def kernel_device_ms(fn, reps: int = 3) -> dict:
+    """Average device time (ms) per call of each kernel launched by fn(), from CUPTI activity
+    records (torch.profiler), after the timed region; keys are the kernels' names."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    out = {}
+    for e in prof.key_averages():
+        t = getattr(e, "device_time_total", None)
+        if t is None:
+            t = getattr(e, "cuda_time_total", 0.0)
+        if t and e.count:
+            out[e.key] = out.get(e.key, 0.0) + t / 1e3 / reps
+    return out
+
+
+def prefill_point(S: int, steps: int, warmup: int, dist, B=8, Hq=32, Hkv=8, D=64, kvd=1):
+    """Causal prefill of B sequences of S tokens, sharded over the ranks (B/N each): RoPE + bf16
+    cache write + attention (tl_prefill_step).  Returns the step time (ms, max over ranks), the
+    device times of the attention kernel and of the RoPE/cache-write prologue (ms, max over
+    ranks), and the whole job's flops."""
     import torch
     from tinylama_b200 import _lib
+    n = dist.world
+    Bl = max(1, B // n)
     h = C.c_void_p()
-    _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, 10000.0, S, B, kvd,
+    _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, 10000.0, S, Bl, kvd,
                                        torch.cuda.current_device()))
     try:
         stream = torch.cuda.Stream()
         torch.cuda.set_stream(stream)
-        g = torch.Generator(device="cuda").manual_seed(S)
-        q = torch.randn(B, S, Hq * D, device="cuda", generator=g)
-        k = torch.randn(B, S, Hkv * D, device="cuda", generator=g)
-        v = torch.randn(B, S, Hkv * D, device="cuda", generator=g)
+        g = torch.Generator(device="cuda").manual_seed(S * 16 + dist.rank)
+        q = torch.randn(Bl, S, Hq * D, device="cuda", generator=g)
+        k = torch.randn(Bl, S, Hkv * D, device="cuda", generator=g)
+        v = torch.randn(Bl, S, Hkv * D, device="cuda", generator=g)
         out = torch.empty_like(q)
         p = lambda t: C.c_void_p(t.data_ptr())
         sp = C.c_void_p(stream.cuda_stream)
 
         def step():
-            _lib.check(_lib.lib.tl_prefill_step(h, 0, 0, B, S, p(q), p(k), p(v), p(out), sp))
+            _lib.check(_lib.lib.tl_prefill_step(h, 0, 0, Bl, S, p(q), p(k), p(v), p(out), sp))
 
-        class _D:
-            def barrier(self): pass
-            def max(self, x): return x
-        ms = time_steps(step, steps, warmup, stream, _D())
+        ms = time_steps(step, steps, warmup, stream, dist)
         _lib.check(_lib.lib.tl_check_device(h, C.c_void_p(stream.cuda_stream)))
-        flops = B * Hq * 2 * D * S * (S + 1)
-        return ms, flops / (ms / 1e3) / 1e12, flops
+        kt = kernel_device_ms(step)
+        core = sum(t for name, t in kt.items() if "prefill_tc_kernel" in name or "prefill_f32_kernel" in name)
+        pro = sum(t for name, t in kt.items() if "rope_append" in name)
+        flops = Bl * n * Hq * 2 * D * S * (S + 1)
+        return ms, dist.max(core), dist.max(pro), flops
     finally:
         _lib.lib.tl_attn_destroy(h)
 
@@ -394,12 +422,20 @@ def run_prefill(args, dist):
     pk = peaks()
     res = {}
     for S in sizes:
-        ms, tf, flops = prefill_point(S, max(5, args.steps // 2), args.warmup)
+        ms, core_ms, pro_ms, flops = prefill_point(S, max(5, args.steps // 2), args.warmup, dist)
+        tf = flops / (ms / 1e3) / 1e12
+        tf_core = flops / (core_ms / 1e3) / 1e12 if core_ms > 0 else None
         res[str(S)] = {"ms_per_step": round(ms, 4), "tflops": round(tf, 1),
-                       "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4), "flops": flops}
-    return {"workload": "causal prefill, 8 sequences, 32 q / 8 kv heads, head_dim 64, bf16 KV "
-                        "(tcgen05), step = RoPE + cache write + attention",
-            "by_seq_len": res, "peak_tflops": pk["bf16_tflops"], "peak_src": pk["src"]}
+                       "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4), "flops": flops,
+                       "attention_core": {"ms": round(core_ms, 4),
+                                          "tflops": None if tf_core is None else round(tf_core, 1),
+                                          "frac_of_bf16_peak": None if tf_core is None else
+                                          round(tf_core / pk["bf16_tflops"], 4)},
+                       "prologue_ms": round(pro_ms, 4)}
+    return {"workload": "causal prefill, 8 sequences (sharded over the GPUs), 32 q / 8 kv heads, head_dim 64, "
+                        "bf16 KV (tcgen05); step = RoPE + cache write + attention (end to end on the device); "
+                        "attention_core = the attention kernel alone (CUPTI device time)",
+            "n_gpus": dist.world, "by_seq_len": res, "peak_tflops": pk["bf16_tflops"], "peak_src": pk["src"]}
 
 
 # ------------------------------------------------------------- TinyLlama decode latency
@@ -565,7 +601,8 @@ def run_reference(args, dist):
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * B / value, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "batched multi-sequence decode (Llama-2-7B-style attention)",
+        "config": {"workload": "batched multi-sequence decode (TinyLlama GQA attention)" if gqa else
+                               "batched multi-sequence decode (Llama-2-7B-style attention)",
                    "seqs_per_gpu": B, "ctx_len": "U[256,4096] seeded", "n_head": Hq, "n_head_kv": Hkv,
                    "head_dim": D, "kv_dtype": "f32"},
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
@@ -582,7 +619,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_batched",
-                    choices=["decode_batched", "decode_batched_bf16", "splitkv", "prefill", "decode_tiny"])
+                    choices=["decode_batched", "decode_batched_bf16", "decode_batched_gqa",
+                             "decode_batched_gqa_bf16", "splitkv", "prefill", "decode_tiny"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the prefill sub-measurement")
     ap.add_argument("--prefill-sizes", default="512,2048,8192", help="sequence lengths of the prefill")
@@ -602,6 +640,10 @@ def main():
             res = run_decode_batched(args, dist, 0)
         elif args.workload == "decode_batched_bf16":
             res = run_decode_batched(args, dist, 1)
+        elif args.workload == "decode_batched_gqa":
+            res = run_decode_batched(args, dist, 0, (32, 4, 64))
+        elif args.workload == "decode_batched_gqa_bf16":
+            res = run_decode_batched(args, dist, 1, (32, 4, 64))
         elif args.workload == "splitkv":
             res = run_splitkv(args, dist)
         elif args.workload == "decode_tiny":
