@@ -376,8 +376,8 @@ int occ_t() {
 
 cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     if (decode_mma_covers(a.headDim, a.nHead / a.nHeadKv, a.kv.dtype)) {
-        // bf16 cache: tensor-core kernel; the CUDA-core kernel below is used only if its tensor
-        // maps cannot be built
+        // bf16 caches, and f32 caches with G >= 4: tensor-core kernel; the CUDA-core kernel
+        // below is used only if its tensor maps cannot be built
         const cudaError_t e = launch_decode_mma(a, num_ctas, s);
         if (e != cudaErrorNotSupported) return e;
     }
@@ -396,15 +396,15 @@ static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype);
 
 int decode_ctas_per_sm(int headDim, int group, int dtype) {
     if (decode_mma_covers(headDim, group, dtype)) {
-        static int mcache[16][2][9];
+        static int mcache[16][2][2][9];
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev >= 0 && dev < 16 && group >= 1 && group <= 8) {
-            int &slot = mcache[dev][headDim == 128][group];
-            if (slot == 0) slot = decode_mma_ctas_per_sm(headDim, group);
+            int &slot = mcache[dev][headDim == 128][dtype == TL_KV_F32][group];
+            if (slot == 0) slot = decode_mma_ctas_per_sm(headDim, group, dtype);
             return slot;
         }
-        return decode_mma_ctas_per_sm(headDim, group);
+        return decode_mma_ctas_per_sm(headDim, group, dtype);
     }
     // occupancy of each kernel instance, queried once per process and device
     static int cache[16][2][2][9];  // [device][headDim 64/128][dtype][group]

@@ -21,6 +21,17 @@
 //        B = V fragments from ldmatrix.trans.
 //  * end of unit: the warps' states go through shared memory to the shared merge
 //    (decode_common.cuh).
+//
+// f32 caches with G >= 4 take the same path (on the CUDA cores such groups need ~G*2 flops per
+// byte, more than the FP32 pipe delivers at HBM speed), on mma.sync.m16n8k8 with tf32 inputs.
+// The f32 tiles arrive through TMA in 32-column boxes (128-byte swizzle); every q, K, V and P
+// value is split in registers into a tf32 "big" part and the tf32 "small" remainder (x = big +
+// small to 2^-22 relative).  q and p put big in fragment rows 0..7 and small in rows 8..15, and
+// each product takes two MMAs (K big, K small; V big, V small), so all four cross terms are
+// kept and the products are as accurate as fp32 ones.  A thread reads whole 16-byte chunks of
+// the swizzled tile (conflict-free), which fixes the head_dim columns it serves: for S the k16
+// block kt takes chunk 2*tq + (kt & 1) of box kt/2, for O the n8 tile nt holds column
+// 32*(nt/4) + 4*n + (nt % 4).  q and the output use the same column order.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -37,16 +48,19 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;
 
-template <int D, int G>
+template <typename KV, int D, int G>
 struct MmaCfg {
+    static constexpr bool F32 = sizeof(KV) == 4;
     static constexpr int T = 64;                     // positions per tile
     static constexpr int NW = 4;                     // consumer warps, 16 positions each
     static constexpr int THREADS = 32 * (NW + 1);
-    static constexpr int HALVES = D / 64;            // 64-column boxes per row
+    static constexpr int BOX_COLS = 128 / (int)sizeof(KV);  // columns per 128-byte box row
+    static constexpr int HALVES = D / BOX_COLS;      // boxes per row
     static constexpr int HALF_BYTES = T * 128;       // one box: 64 rows x 128 B
     static constexpr int TILE_BYTES = HALVES * HALF_BYTES;
     static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-    static constexpr int NS = D == 128 ? 3 : 4;
+    static constexpr int NS = F32 ? (D == 128 ? 2 : 3) : (D == 128 ? 3 : 4);
+    static constexpr int MIN_CTAS = (F32 && D == 128) ? 1 : 2;  // resident CTAs per SM (register cap)
     static constexpr int KT = D / 16;                // k16 steps over head_dim
     static constexpr int NT = D / 8;                 // n8 tiles over head_dim
     static constexpr int OFF_STAGES = 0;             // 1024-aligned (swizzle atoms)
@@ -102,16 +116,33 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_
     lo = pack2(x0 - __low2float(h), x1 - __high2float(h));
 }
 
+// D += A * B, m16n8k8, tf32 inputs, fp32 accumulators (f32 caches).  A rows 0..7 carry the
+// tf32 "big" part of q (or p), rows 8..15 the "small" remainder.
+__device__ __forceinline__ void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// tf32 big/small split: x = big + small + e with |e| <= 2^-22 |x| (big, small: tf32 bit patterns)
+__device__ __forceinline__ void split_tf32(float x, uint32_t &big, uint32_t &small) {
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(big) : "f"(x));
+    const float r = x - __uint_as_float(big);
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(small) : "f"(r));
+}
+
 // address of 16-byte chunk `chunk` (0..7) of row `row` in a swizzled 64-column box
 __device__ __forceinline__ uint32_t swz(uint32_t box, int row, int chunk) {
     return box + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
-template <int D, int G>
-__global__ void __launch_bounds__(MmaCfg<D, G>::THREADS)
+template <typename KV, int D, int G>
+__global__ void __launch_bounds__(MmaCfg<KV, D, G>::THREADS, MmaCfg<KV, D, G>::MIN_CTAS)
 decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const DecodeArgs a) {
-    using C = MmaCfg<D, G>;
+    using C = MmaCfg<KV, D, G>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -163,8 +194,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
 #pragma unroll
                     for (int hh = 0; hh < C::HALVES; ++hh) {
-                        tma_load_2d(st + hh * C::HALF_BYTES, &kmap, 64 * hh, row0 + p, &full[stage], pol);
-                        tma_load_2d(st + C::TILE_BYTES + hh * C::HALF_BYTES, &vmap, 64 * hh, row0 + p, &full[stage], pol);
+                        tma_load_2d(st + hh * C::HALF_BYTES, &kmap, C::BOX_COLS * hh, row0 + p, &full[stage], pol);
+                        tma_load_2d(st + C::TILE_BYTES + hh * C::HALF_BYTES, &vmap, C::BOX_COLS * hh, row0 + p,
+                                    &full[stage], pol);
                     }
                     ++issued;
                     if (++stage == C::NS) { stage = 0; phase ^= 1u; }
@@ -190,20 +222,30 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     uint32_t phase = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
         const Unit un = decode_unit(a, prefix, lens, u);
-        // q fragments (A rows = heads of this kv group; rows >= G are zero), bf16 hi + lo
-        uint32_t qh[C::KT][2], ql[C::KT][2];
+        // q fragments (A rows = heads of this kv group; rows >= G are zero): bf16 hi + lo for
+        // bf16 caches; tf32 big + small of the four columns of one chunk per k16 block for f32
+        uint32_t qh[C::KT][C::F32 ? 4 : 2], ql[C::KT][C::F32 ? 4 : 2];
         {
             const float *qrow = a.q + ((int64_t)un.b * a.nHead + (int64_t)un.g * G + (row_ok ? gid : 0)) * D;
 #pragma unroll
             for (int kt = 0; kt < C::KT; ++kt) {
-                float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
-                if (row_ok) {
-                    const float2 lo = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq);
-                    const float2 hi = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq + 8);
-                    x0 = lo.x; x1 = lo.y; x2 = hi.x; x3 = hi.y;
+                if constexpr (C::F32) {
+                    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (row_ok) x = *reinterpret_cast<const float4 *>(qrow + 32 * (kt >> 1) + 4 * (2 * tq + (kt & 1)));
+                    split_tf32(x.x, qh[kt][0], ql[kt][0]);
+                    split_tf32(x.y, qh[kt][1], ql[kt][1]);
+                    split_tf32(x.z, qh[kt][2], ql[kt][2]);
+                    split_tf32(x.w, qh[kt][3], ql[kt][3]);
+                } else {
+                    float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+                    if (row_ok) {
+                        const float2 lo = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq);
+                        const float2 hi = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq + 8);
+                        x0 = lo.x; x1 = lo.y; x2 = hi.x; x3 = hi.y;
+                    }
+                    split2(x0, x1, qh[kt][0], ql[kt][0]);
+                    split2(x2, x3, qh[kt][1], ql[kt][1]);
                 }
-                split2(x0, x1, qh[kt][0], ql[kt][0]);
-                split2(x2, x3, qh[kt][1], ql[kt][1]);
             }
         }
         float m = -INFINITY, l = 0.f;
@@ -219,7 +261,30 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             const int r0 = warp * 16;  // first tile row of this warp
             // ---- S = Q K^T for 16 positions: two n8 tiles ----
             float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            {
+            if constexpr (C::F32) {
+                // B[k][n] = K[position r0 + 8*nt + gid][column]: one 16-byte read per (k16 block,
+                // n8 tile) covers two k8 steps (k = tq, tq+4 <- columns d0, d0+1, then d0+2,
+                // d0+3); K big and K small each take one MMA per step
+#pragma unroll
+                for (int kt = 0; kt < C::KT; ++kt) {
+                    const uint32_t box = kbox + (kt >> 1) * C::HALF_BYTES;
+                    const int chunk = 2 * tq + (kt & 1);
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        const float4 x = *reinterpret_cast<const float4 *>(
+                            smem_raw + (swz(box, r0 + 8 * nt + gid, chunk) - raw));
+                        uint32_t kb[4], ks[4];
+                        split_tf32(x.x, kb[0], ks[0]);
+                        split_tf32(x.y, kb[1], ks[1]);
+                        split_tf32(x.z, kb[2], ks[2]);
+                        split_tf32(x.w, kb[3], ks[3]);
+                        mma1688(s[nt], qh[kt][0], ql[kt][0], qh[kt][1], ql[kt][1], kb[0], kb[1]);
+                        mma1688(s[nt], qh[kt][0], ql[kt][0], qh[kt][1], ql[kt][1], ks[0], ks[1]);
+                        mma1688(s[nt], qh[kt][2], ql[kt][2], qh[kt][3], ql[kt][3], kb[2], kb[3]);
+                        mma1688(s[nt], qh[kt][2], ql[kt][2], qh[kt][3], ql[kt][3], ks[2], ks[3]);
+                    }
+                }
+            } else {
                 const int krow = r0 + ((lane >> 4) << 3) + (lane & 7);  // n tile = lane >> 4
                 const int kc = (lane >> 3) & 1;                          // 8-dim half of the k16 step
 #pragma unroll
@@ -264,10 +329,41 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             ps += __shfl_xor_sync(0xffffffffu, ps, 2);
             l += ps;
             // ---- O += P V: P as the A fragment (k = the 16 positions), hi + lo ----
-            uint32_t ph0, pl0, ph1, pl1;
-            split2(pr[0], pr[1], ph0, pl0);  // row gid, k = 2tq, 2tq+1
-            split2(pr[2], pr[3], ph1, pl1);  // row gid, k = 2tq+8, 2tq+9
-            {
+            if constexpr (C::F32) {
+                // tf32 k8 steps over positions: step 0 maps k = tq, tq+4 to this thread's
+                // positions 2tq, 2tq+1 of n8 tile 0 of S, step 1 to 8+2tq, 9+2tq (so P stays
+                // where S left it).  B[k][n] = V[that position][column of n8 tile nt, n = gid]: a
+                // 16-byte read of chunk gid of box j at one position gives n = gid of tiles
+                // 4j .. 4j+3.  V big and V small each take one MMA per step.
+                uint32_t pb[4], ps[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) split_tf32(pr[i], pb[i], ps[i]);
+#pragma unroll
+                for (int j = 0; j < C::HALVES; ++j) {
+                    const uint32_t box = vbox + j * C::HALF_BYTES;
+                    const float4 x0 = *reinterpret_cast<const float4 *>(smem_raw + (swz(box, r0 + 2 * tq, gid) - raw));
+                    const float4 x1 = *reinterpret_cast<const float4 *>(smem_raw + (swz(box, r0 + 2 * tq + 1, gid) - raw));
+                    const float4 x8 = *reinterpret_cast<const float4 *>(smem_raw + (swz(box, r0 + 2 * tq + 8, gid) - raw));
+                    const float4 x9 = *reinterpret_cast<const float4 *>(smem_raw + (swz(box, r0 + 2 * tq + 9, gid) - raw));
+                    const float a0[4] = {x0.x, x0.y, x0.z, x0.w}, a1[4] = {x1.x, x1.y, x1.z, x1.w};
+                    const float a8[4] = {x8.x, x8.y, x8.z, x8.w}, a9[4] = {x9.x, x9.y, x9.z, x9.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        uint32_t v0b, v0s, v1b, v1s, v8b, v8s, v9b, v9s;
+                        split_tf32(a0[u], v0b, v0s);
+                        split_tf32(a1[u], v1b, v1s);
+                        split_tf32(a8[u], v8b, v8s);
+                        split_tf32(a9[u], v9b, v9s);
+                        mma1688(o[4 * j + u], pb[0], ps[0], pb[1], ps[1], v0b, v1b);
+                        mma1688(o[4 * j + u], pb[0], ps[0], pb[1], ps[1], v0s, v1s);
+                        mma1688(o[4 * j + u], pb[2], ps[2], pb[3], ps[3], v8b, v9b);
+                        mma1688(o[4 * j + u], pb[2], ps[2], pb[3], ps[3], v8s, v9s);
+                    }
+                }
+            } else {
+                uint32_t ph0, pl0, ph1, pl1;
+                split2(pr[0], pr[1], ph0, pl0);  // row gid, k = 2tq, 2tq+1
+                split2(pr[2], pr[3], ph1, pl1);  // row gid, k = 2tq+8, 2tq+9
                 const int vrow = r0 + (((lane >> 3) & 1) << 3) + (lane & 7);
                 const int vc = lane >> 4;  // which n8 tile of the pair
 #pragma unroll
@@ -291,9 +387,15 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             }
 #pragma unroll
             for (int nt = 0; nt < C::NT; ++nt) {
-                float *dst = wo + (warp * G + gid) * D + 8 * nt + 2 * tq;
-                dst[0] = o[nt][0] + o[nt][2];  // hi rows + lo rows
-                dst[1] = o[nt][1] + o[nt][3];
+                float *row = wo + (warp * G + gid) * D;
+                if constexpr (C::F32) {
+                    const int c = 32 * (nt >> 2) + (nt & 3);  // column of n = 2tq is c + 8tq
+                    row[c + 8 * tq] = o[nt][0] + o[nt][2];       // hi rows + lo rows
+                    row[c + 8 * tq + 4] = o[nt][1] + o[nt][3];
+                } else {
+                    row[8 * nt + 2 * tq] = o[nt][0] + o[nt][2];  // hi rows + lo rows
+                    row[8 * nt + 2 * tq + 1] = o[nt][1] + o[nt][3];
+                }
             }
         }
         unit_epilogue<G, D, C::NW>(a, un, u, prefix, wm, wl, wo, cw, is_last_flag, tid, warp, lane);
@@ -316,28 +418,32 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
-// 2-D map over a whole bf16 cache: rows = layer*slot*kvHead*pos, D columns; box 64 x 64.
-bool make_cache_map(CUtensorMap *m, const void *ptr, uint64_t rows, int D) {
+// 2-D map over a whole cache: rows = layer*slot*kvHead*pos, D columns; box = 128 bytes of
+// columns (64 bf16 or 32 f32) x 64 rows.
+bool make_cache_map(CUtensorMap *m, const void *ptr, uint64_t rows, int D, bool f32) {
     auto enc = get_encode();
     if (!enc) return false;
+    const int es = f32 ? 4 : 2;
     cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-    cuuint32_t box[2] = {64, 64};
+    cuuint64_t strides[1] = {(cuuint64_t)D * es};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / es), 64};
     cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+    return enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+               const_cast<void *>(ptr), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D, int G>
+template <typename KV, int D, int G>
 cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
-    using C = MmaCfg<D, G>;
+    using C = MmaCfg<KV, D, G>;
     const uint64_t rows = (uint64_t)a.kv.nLayer * a.kv.maxBatch * a.kv.nHeadKv * a.kv.maxLen;
     if (rows + C::T > (uint64_t)INT32_MAX) return cudaErrorNotSupported;
     CUtensorMap km, vm;
-    if (!make_cache_map(&km, a.kv.k, rows, D) || !make_cache_map(&vm, a.kv.v, rows, D)) return cudaErrorNotSupported;
+    if (!make_cache_map(&km, a.kv.k, rows, D, C::F32) || !make_cache_map(&vm, a.kv.v, rows, D, C::F32))
+        return cudaErrorNotSupported;
     const size_t smem = C::smem_bytes(a.nseq);
-    auto kern = decode_mma_kernel<D, G>;
+    auto kern = decode_mma_kernel<KV, D, G>;
     // only when it grows (per device): steady-state launches make no attribute calls
     static size_t smem_set[64] = {};
     int dev = 0;
@@ -352,13 +458,13 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-template <int D, int G>
+template <typename KV, int D, int G>
 int occ_t() {
-    using C = MmaCfg<D, G>;
+    using C = MmaCfg<KV, D, G>;
     int n = 0;
     const size_t smem = C::smem_bytes(256);
-    cudaFuncSetAttribute(decode_mma_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<D, G>, C::THREADS, smem) != cudaSuccess)
+    cudaFuncSetAttribute(decode_mma_kernel<KV, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<KV, D, G>, C::THREADS, smem) != cudaSuccess)
         n = 1;
     return n < 1 ? 1 : n;
 }
@@ -366,38 +472,57 @@ int occ_t() {
 }  // namespace
 
 bool decode_mma_covers(int headDim, int group, int dtype) {
-    return dtype == TL_KV_BF16 && (headDim == 64 || headDim == 128) &&
-           (group == 1 || group == 2 || group == 4 || group == 8);
+    if (headDim != 64 && headDim != 128) return false;
+    if (dtype == TL_KV_BF16) return group == 1 || group == 2 || group == 4 || group == 8;
+    // f32: the CUDA-core kernel stays at the HBM roofline up to G = 2
+    return dtype == TL_KV_F32 && (group == 4 || group == 8);
 }
 
 cudaError_t launch_decode_mma(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     const int G = a.nHead / a.nHeadKv;
-#define TL_MMA_CASE(DD)                                           \
-    switch (G) {                                                  \
-        case 1: return launch_t<DD, 1>(a, num_ctas, s);           \
-        case 2: return launch_t<DD, 2>(a, num_ctas, s);           \
-        case 4: return launch_t<DD, 4>(a, num_ctas, s);           \
-        case 8: return launch_t<DD, 8>(a, num_ctas, s);           \
-        default: return cudaErrorNotSupported;                    \
+    if (!decode_mma_covers(a.headDim, G, a.kv.dtype)) return cudaErrorNotSupported;
+#define TL_MMA_CASE(DD)                                                     \
+    switch (G) {                                                            \
+        case 1: return launch_t<__nv_bfloat16, DD, 1>(a, num_ctas, s);      \
+        case 2: return launch_t<__nv_bfloat16, DD, 2>(a, num_ctas, s);      \
+        case 4: return launch_t<__nv_bfloat16, DD, 4>(a, num_ctas, s);      \
+        case 8: return launch_t<__nv_bfloat16, DD, 8>(a, num_ctas, s);      \
+        default: return cudaErrorNotSupported;                              \
     }
-    if (a.kv.dtype != TL_KV_BF16) return cudaErrorNotSupported;
-    if (a.headDim == 64) { TL_MMA_CASE(64) }
-    if (a.headDim == 128) { TL_MMA_CASE(128) }
+#define TL_MMA_CASE_F32(DD)                                                 \
+    switch (G) {                                                            \
+        case 4: return launch_t<float, DD, 4>(a, num_ctas, s);              \
+        case 8: return launch_t<float, DD, 8>(a, num_ctas, s);              \
+        default: return cudaErrorNotSupported;                              \
+    }
+    if (a.kv.dtype == TL_KV_F32) {
+        if (a.headDim == 64) { TL_MMA_CASE_F32(64) }
+        if (a.headDim == 128) { TL_MMA_CASE_F32(128) }
+    } else {
+        if (a.headDim == 64) { TL_MMA_CASE(64) }
+        if (a.headDim == 128) { TL_MMA_CASE(128) }
+    }
 #undef TL_MMA_CASE
+#undef TL_MMA_CASE_F32
     return cudaErrorNotSupported;
 }
 
-int decode_mma_ctas_per_sm(int headDim, int group) {
-#define TL_MMA_OCC(DD)                         \
-    switch (group) {                           \
-        case 1: return occ_t<DD, 1>();         \
-        case 2: return occ_t<DD, 2>();         \
-        case 4: return occ_t<DD, 4>();         \
-        case 8: return occ_t<DD, 8>();         \
-        default: return 1;                     \
+int decode_mma_ctas_per_sm(int headDim, int group, int dtype) {
+#define TL_MMA_OCC(KV, DD)                         \
+    switch (group) {                               \
+        case 1: return occ_t<KV, DD, 1>();         \
+        case 2: return occ_t<KV, DD, 2>();         \
+        case 4: return occ_t<KV, DD, 4>();         \
+        case 8: return occ_t<KV, DD, 8>();         \
+        default: return 1;                         \
     }
-    if (headDim == 64) { TL_MMA_OCC(64) }
-    if (headDim == 128) { TL_MMA_OCC(128) }
+    if (dtype == TL_KV_F32) {
+        if (headDim == 64) return group == 8 ? occ_t<float, 64, 8>() : occ_t<float, 64, 4>();
+        if (headDim == 128) return group == 8 ? occ_t<float, 128, 8>() : occ_t<float, 128, 4>();
+    } else {
+        if (headDim == 64) { TL_MMA_OCC(__nv_bfloat16, 64) }
+        if (headDim == 128) { TL_MMA_OCC(__nv_bfloat16, 128) }
+    }
 #undef TL_MMA_OCC
     return 1;
 }

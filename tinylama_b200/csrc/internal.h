@@ -145,7 +145,7 @@ int decode_ctas_per_sm(int headDim, int group, int dtype);
 // tensor-core decode for bf16 caches (decode_mma.cu)
 bool decode_mma_covers(int headDim, int group, int dtype);
 cudaError_t launch_decode_mma(const DecodeArgs &a, int num_ctas, cudaStream_t s);
-int decode_mma_ctas_per_sm(int headDim, int group);
+int decode_mma_ctas_per_sm(int headDim, int group, int dtype);
 size_t decode_partial_floats(int total_units, int group, int headDim);
 
 // Merge G per-rank (o, m, l) partials [G][nseq][nHead][d+2] into out [nseq][nHead][d].
