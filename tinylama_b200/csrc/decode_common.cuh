@@ -16,7 +16,9 @@
 
 namespace tl {
 
-constexpr int kMaxChunksPerSeq = 256;
+// chunks per sequence in one launch: the planners stay within it (64), and the merge
+// weights of a sequence's chunks take kMaxChunksPerSeq * G floats of shared memory
+constexpr int kMaxChunksPerSeq = 64;
 
 __device__ __forceinline__ float safe_exp2_diff(float m, float M) {
     return (m == -INFINITY) ? 0.f : exp2f(m - M);

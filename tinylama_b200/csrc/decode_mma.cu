@@ -59,8 +59,14 @@ struct MmaCfg {
     static constexpr int HALF_BYTES = T * 128;       // one box: 64 rows x 128 B
     static constexpr int TILE_BYTES = HALVES * HALF_BYTES;
     static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-    static constexpr int NS = F32 ? (D == 128 ? 2 : 3) : (D == 128 ? 3 : 4);
-    static constexpr int MIN_CTAS = (F32 && D == 128) ? 1 : 2;  // resident CTAs per SM (register cap)
+#ifndef TL_NS_BF16_64
+#define TL_NS_BF16_64 3
+#endif
+#ifndef TL_MIN_BF16_64
+#define TL_MIN_BF16_64 2
+#endif
+    static constexpr int NS = F32 ? 2 : (D == 128 ? 3 : TL_NS_BF16_64);
+    static constexpr int MIN_CTAS = (F32 && D == 128) ? 1 : ((!F32 && D == 64) ? TL_MIN_BF16_64 : 2);  // register cap
     static constexpr int KT = D / 16;                // k16 steps over head_dim
     static constexpr int NT = D / 8;                 // n8 tiles over head_dim
     static constexpr int OFF_STAGES = 0;             // 1024-aligned (swizzle atoms)

@@ -43,7 +43,7 @@ constexpr size_t kCounterBytes = sizeof(unsigned) * kNoAllocCounters;  // 256 Ki
 constexpr size_t kErrBytes = 256;
 constexpr size_t kPartialOffset = kCounterBytes + kErrBytes;
 constexpr size_t kPartialFloats = (kNoAllocBytes - kPartialOffset) / sizeof(float);
-constexpr int kMaxChunksPerSeq = 256;
+constexpr int kMaxChunksPerSeq = 64;  // the decode kernels' limit (decode_common.cuh)
 constexpr int kMaxDevices = 64;
 
 // The scratch.  Host code must not take this name's address: on the host it is only a
