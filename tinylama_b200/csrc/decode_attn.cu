@@ -49,7 +49,8 @@ struct DecCfg {
     // shared memory carve-up (bytes, all 16-aligned)
     static constexpr int OFF_STAGES = 0;
     static constexpr int OFF_BARS = OFF_STAGES + NS * STAGE_BYTES;
-    static constexpr int OFF_SC = OFF_BARS + 2 * NS * 8 + 16;           // [NW][NV] scores
+    static constexpr int OFF_UQ = OFF_BARS + 2 * NS * 8 + 16;           // unit queue
+    static constexpr int OFF_SC = OFF_UQ + kUnitQBytes;                 // [NW][NV] scores
     static constexpr int OFF_WM = OFF_SC + NW * NV * 4;                 // [NW][G] m
     static constexpr int OFF_WL = OFF_WM + NW * G * 4;                  // [NW][G] l
     static constexpr int OFF_WO = OFF_WL + NW * G * 4;                  // [NW][G][D] o
@@ -113,6 +114,7 @@ decode_kernel(const DecodeArgs a) {
     int *prefix = reinterpret_cast<int *>(smem + C::OFF_PREFIX);
     // lens are kept in the high part of the prefix region: prefix[nseq+1], lens after it
     int *lens = prefix + (a.nseq + 1);
+    UnitQueue *uq = reinterpret_cast<UnitQueue *>(smem + C::OFF_UQ);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned *err = a.err;
@@ -122,6 +124,10 @@ decode_kernel(const DecodeArgs a) {
         for (int s = 0; s < C::NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], C::NW);
+        }
+        for (int s = 0; s < kUnitQ; ++s) {
+            mbar_init(&uq->full[s], 1);
+            mbar_init(&uq->empty[s], C::NW);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -145,7 +151,11 @@ decode_kernel(const DecodeArgs a) {
             uint32_t phase = 0;
             long issued = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+            int qs = 0, u = 0;
+            uint32_t qp = 0;
+            while (ok) {
+                if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, err, abort_flag)) { ok = false; break; }
+                if (u < 0) break;
                 const Unit un = decode_unit(a, prefix, lens, u);
                 const int64_t row0 = a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
                 const KV *kb = reinterpret_cast<const KV *>(a.kv.k) + row0 * D;
@@ -162,6 +172,7 @@ decode_kernel(const DecodeArgs a) {
                     if (++stage == C::NS) { stage = 0; phase ^= 1u; }
                 }
             }
+            if (ok) unitq_finish(a);
             if (!ok) {
                 // drain: wait (bounded) for the copies this thread issued into the ring
                 const int outstanding = issued < (long)C::NS ? (int)issued : C::NS;
@@ -179,7 +190,11 @@ decode_kernel(const DecodeArgs a) {
     // ================= consumers ==================
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+    int qs = 0;
+    uint32_t qp = 0;
+    while (true) {
+        const int u = unitq_pop(uq, qs, qp, err, abort_flag, lane);
+        if (u < 0) break;
         const Unit un = decode_unit(a, prefix, lens, u);
         // q for the G heads of this group, pre-scaled so that scores are in log2 units
         float qf[G][C::VPL];

@@ -68,6 +68,71 @@ __device__ __forceinline__ Unit decode_unit(const DecodeArgs &a, const int *pref
     return r;
 }
 
+// ---- dynamic unit schedule ---------------------------------------------------------------
+// The producer warp of each CTA claims units from a.work[0] and hands their ids to the
+// consumer warps through a small queue in shared memory (full/empty mbarriers), so a CTA that
+// drew short units takes more of them.  Claims follow a rank order that puts every sequence's
+// chunks before its last one first and the sequences' last chunks (the only partial ones)
+// after them, so the units left for the final claims are the short ones.  The producer that
+// finishes last resets the counters for the next launch.
+constexpr int kUnitQ = 4;
+struct UnitQueue {
+    uint64_t full[kUnitQ], empty[kUnitQ];
+    int id[kUnitQ];
+};
+constexpr int kUnitQBytes = (int)((sizeof(UnitQueue) + 15) / 16 * 16);
+
+// Canonical unit index ((prefix[b] + c) * nHeadKv + g) of claim rank k.
+__device__ __forceinline__ int unit_of_rank(const DecodeArgs &a, const int *prefix, int k) {
+    const int H = a.nHeadKv;
+    const int lead = (prefix[a.nseq] - a.nseq) * H;  // units of chunks other than a sequence's last
+    if (k < lead) {
+        const int t = k / H, g = k - t * H;
+        // sequence b with prefix[b] - b <= t < prefix[b+1] - (b+1): the largest b with prefix[b] - b <= t
+        int lo = 0, hi = a.nseq;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (prefix[mid] - mid <= t) lo = mid; else hi = mid;
+        }
+        return (prefix[lo] + (t - (prefix[lo] - lo))) * H + g;
+    }
+    const int r = k - lead;
+    const int b = r / H, g = r - b * H;
+    return (prefix[b + 1] - 1) * H + g;  // last chunk of sequence b
+}
+
+// Producer (one thread): claim the next unit and publish it; -1 when none remain.  Returns
+// false if the wait for a free queue slot gave up (abort or timeout).
+__device__ __forceinline__ bool unitq_push(const DecodeArgs &a, UnitQueue *q, const int *prefix, int total_units,
+                                           int &slot, uint32_t &phase, int &u, unsigned *err,
+                                           volatile int *abort_flag) {
+    const int k = (int)atomicAdd(a.work, 1u);
+    u = k < total_units ? unit_of_rank(a, prefix, k) : -1;
+    if (!mbar_wait(&q->empty[slot], phase ^ 1u, err, abort_flag)) return false;
+    q->id[slot] = u;
+    mbar_arrive(&q->full[slot]);
+    if (++slot == kUnitQ) { slot = 0; phase ^= 1u; }
+    return true;
+}
+// Producer, after publishing its -1: the last producer of the launch resets the counters.
+__device__ __forceinline__ void unitq_finish(const DecodeArgs &a) {
+    __threadfence();
+    if (atomicAdd(a.work + 1, 1u) == gridDim.x - 1) {
+        atomicExch(a.work, 0u);
+        atomicExch(a.work + 1, 0u);
+    }
+}
+// Consumer warp: the next unit id (the same for every lane), -1 at the end or on abort.
+__device__ __forceinline__ int unitq_pop(UnitQueue *q, int &slot, uint32_t &phase, unsigned *err,
+                                         volatile int *abort_flag, int lane) {
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&q->full[slot], phase, err, abort_flag));
+    const int u = ok ? *reinterpret_cast<volatile int *>(&q->id[slot]) : -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&q->empty[slot]);
+    if (++slot == kUnitQ) { slot = 0; phase ^= 1u; }
+    return u;
+}
+
 // Warp 0: per-sequence local lengths, chunk counts and their exclusive prefix.
 __device__ __forceinline__ void build_schedule(const DecodeArgs &a, int *prefix, int *lens, int *max_nch,
                                                int lane, unsigned *err) {

@@ -71,7 +71,8 @@ struct MmaCfg {
     static constexpr int NT = D / 8;                 // n8 tiles over head_dim
     static constexpr int OFF_STAGES = 0;             // 1024-aligned (swizzle atoms)
     static constexpr int OFF_BARS = NS * STAGE_BYTES;
-    static constexpr int OFF_WM = OFF_BARS + 2 * NS * 8 + 16;
+    static constexpr int OFF_UQ = OFF_BARS + 2 * NS * 8 + 16;  // unit queue
+    static constexpr int OFF_WM = OFF_UQ + kUnitQBytes;
     static constexpr int OFF_WL = OFF_WM + NW * G * 4;
     static constexpr int OFF_WO = OFF_WL + NW * G * 4;
     static constexpr int OFF_CW = OFF_WO + NW * G * D * 4;
@@ -163,6 +164,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     float *cw = reinterpret_cast<float *>(smem + C::OFF_CW);
     int *prefix = reinterpret_cast<int *>(smem + C::OFF_PREFIX);
     int *lens = prefix + (a.nseq + 1);
+    UnitQueue *uq = reinterpret_cast<UnitQueue *>(smem + C::OFF_UQ);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned *err = a.err;
@@ -170,6 +172,10 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
         for (int s = 0; s < C::NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], C::NW);
+        }
+        for (int s = 0; s < kUnitQ; ++s) {
+            mbar_init(&uq->full[s], 1);
+            mbar_init(&uq->empty[s], C::NW);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -191,7 +197,11 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             uint32_t phase = 0;
             long issued = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+            int qs = 0, u = 0;
+            uint32_t qp = 0;
+            while (ok) {
+                if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, err, abort_flag)) { ok = false; break; }
+                if (u < 0) break;
                 const Unit un = decode_unit(a, prefix, lens, u);
                 const int row0 = (int)a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
                 for (int p = un.p0; p < un.p1; p += C::T) {
@@ -208,6 +218,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                     if (++stage == C::NS) { stage = 0; phase ^= 1u; }
                 }
             }
+            if (ok) unitq_finish(a);
             // wait (bounded) for every copy issued into this CTA's shared memory
             const int outstanding = issued < (long)C::NS ? (int)issued : C::NS;
             int s = stage;
@@ -226,7 +237,11 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     const float C2 = kLog2e / sqrtf((float)D);
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+    int qs = 0;
+    uint32_t qp = 0;
+    while (true) {
+        const int u = unitq_pop(uq, qs, qp, err, abort_flag, lane);
+        if (u < 0) break;
         const Unit un = decode_unit(a, prefix, lens, u);
         // q fragments (A rows = heads of this kv group; rows >= G are zero): bf16 hi + lo for
         // bf16 caches; tf32 big + small of the four columns of one chunk per k16 block for f32

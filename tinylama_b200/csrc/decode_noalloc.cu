@@ -163,6 +163,7 @@ extern "C" int tl_decode_attention_noalloc(const float *q, const void *k_cache, 
     a.partial_cap = kPartialFloats;
     a.counter = reinterpret_cast<unsigned *>(base);
     a.err = reinterpret_cast<unsigned *>(base + kCounterBytes);
+    a.work = reinterpret_cast<unsigned *>(base + kCounterBytes + 16);  // inside the cleared error block
     a.lse_out = nullptr;
     e = launch_decode(a, (int)std::max<long long>(1, std::min<long long>(units, ctas)), s);
     if (e == cudaErrorNotSupported) return api_fail(TL_ERR_UNSUPPORTED, "decode: shape not covered");

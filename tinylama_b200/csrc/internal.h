@@ -64,7 +64,7 @@ struct tl_attn {
     // arrival counters used by the last CTA of a sequence to merge its chunks.
     float *dPartial = nullptr;
     size_t partialCap = 0;          // floats
-    unsigned *dCounter = nullptr;   // [maxBatch * nHeadKv], zero between launches
+    unsigned *dCounter = nullptr;   // [maxBatch * nHeadKv] + 2 work counters, zero between launches
     // host-tier staging (device side) for q/k/v/ctx copies
     float *dIo = nullptr;
     size_t ioCap = 0;               // floats
@@ -124,6 +124,7 @@ struct DecodeArgs {
     float *partial;        // scratch
     size_t partial_cap;    // floats
     unsigned *counter;     // [nseq * nHeadKv] zeroed
+    unsigned *work;        // [2] zeroed: next unit to claim, producers done (reset by the last)
     unsigned *err;
     // When non-null the kernel writes un-normalised (m, l, o) per (seq, head) here instead
     // of the final output: [nseq][nHead][headDim + 2] = (o[0..d), m, l).

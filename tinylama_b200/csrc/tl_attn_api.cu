@@ -200,6 +200,7 @@ int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, c
     a.partial = h->dPartial;
     a.partial_cap = h->partialCap;
     a.counter = h->dCounter + (size_t)slot0 * h->nHeadKv;
+    a.work = h->dCounter + (size_t)h->maxBatch * h->nHeadKv;
     a.err = h->dErr;
     a.lse_out = lse_out;
     if (px) a.px = *px;
@@ -223,7 +224,7 @@ int finish(tl_attn *h, cudaStream_t s) {
     TL_CUDA(cudaStreamSynchronize(s));
     if (word) {
         cudaMemsetAsync(h->dErr, 0, sizeof(unsigned), s);
-        cudaMemsetAsync(h->dCounter, 0, sizeof(unsigned) * (size_t)h->maxBatch * h->nHeadKv, s);
+        cudaMemsetAsync(h->dCounter, 0, sizeof(unsigned) * ((size_t)h->maxBatch * h->nHeadKv + 2), s);
         cudaStreamSynchronize(s);
         std::string bits;
         if (word & TL_DEVERR_POS_RANGE) bits += " position-out-of-range";
@@ -343,8 +344,8 @@ int tl_attn_create(tl_attn **out, int nLayer, int nHead, int nHeadKv, int headDi
         (e = cudaMalloc(&h->dPos, sizeof(int) * (size_t)maxBatch)) != cudaSuccess ||
         (e = cudaMalloc(&h->dErr, sizeof(unsigned) * 4)) != cudaSuccess ||
         (e = cudaMemset(h->dErr, 0, sizeof(unsigned) * 4)) != cudaSuccess ||
-        (e = cudaMalloc(&h->dCounter, sizeof(unsigned) * (size_t)maxBatch * nHeadKv)) != cudaSuccess ||
-        (e = cudaMemset(h->dCounter, 0, sizeof(unsigned) * (size_t)maxBatch * nHeadKv)) != cudaSuccess ||
+        (e = cudaMalloc(&h->dCounter, sizeof(unsigned) * ((size_t)maxBatch * nHeadKv + 2))) != cudaSuccess ||
+        (e = cudaMemset(h->dCounter, 0, sizeof(unsigned) * ((size_t)maxBatch * nHeadKv + 2))) != cudaSuccess ||
         (e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaDeviceSynchronize()) != cudaSuccess)
         return cleanup(fail(TL_ERR_CUDA, "handle setup failed: %s", cudaGetErrorString(e)));
