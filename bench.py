@@ -49,12 +49,19 @@ def peaks():
             "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
-def traffic_from_profiles(kernel_key: str):
+def traffic_from_profiles(kernel_key: str, algorithmic_bytes: int = 0):
+    """DRAM bytes per launch from the committed ncu summaries: the captured figure, or the
+    captured ratio to the algorithmic bytes times this launch's algorithmic bytes."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
     d = json.load(open(p)).get(kernel_key)
-    return None if d is None else d.get("dram_bytes_per_launch")
+    if d is None:
+        return None
+    if d.get("dram_bytes_per_launch") is not None:
+        return d["dram_bytes_per_launch"]
+    r = d.get("ratio_to_algorithmic")
+    return None if r is None or not algorithmic_bytes else int(r * algorithmic_bytes)
 
 
 class ClockSampler:
@@ -324,7 +331,8 @@ def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
     achieved = w.algorithmic_bytes_attention() / (ms_attn / 1e3) / 1e9
     e2e_dt, h2d, d2h = w.e2e(max(3, args.steps // 4), 2, dist)
     e2e_value = n * w.B / e2e_dt
-    traffic = traffic_from_profiles(("decode_kernel_f32" if kvd == 0 else "decode_kernel_bf16") + ("_gqa" if gqa else ""))
+    traffic = traffic_from_profiles(("decode_kernel_f32" if kvd == 0 else "decode_kernel_bf16") + ("_gqa" if gqa else ""),
+                                    w.algorithmic_bytes_attention())
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": n, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
@@ -341,7 +349,7 @@ def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
         "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "api": "tl_decode_batch_host (pinned host buffers)"},
         "gpu_launches": w.launches_per_step * args.steps,
-        "roofline": {"kernel": "decode_kernel", "bound": "hbm", "achieved": round(achieved, 1),
+        "roofline": {"kernel": "decode_mma_kernel" if (gqa or kvd == 1) else "decode_kernel", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                      "peak_src": pk["src"], "traffic": traffic,
                      "algorithmic_bytes_per_launch": w.algorithmic_bytes_attention(),
