@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -220,7 +221,7 @@ struct TcShape {
     __host__ __device__ static constexpr int col_s(int q) { return q * BN_; }
     __host__ __device__ static constexpr int col_p(int q) { return COL_P0 + q * (BN_ / 2); }
     __host__ __device__ static constexpr int col_o(int q) { return COL_O0 + q * 64; }
-    static constexpr int SMEM = NQ * TILE_BYTES + NS * 2 * KV_TILE;  // + barriers
+    static constexpr int SMEM = 2 * NQ * TILE_BYTES + NS * 2 * KV_TILE;  // two Q buffers + K/V ring (+ barriers)
 };
 
 constexpr int TMEM_ALL = 512;
@@ -303,58 +304,82 @@ constexpr int kPolyMod = TL_POLY_MOD;
 
 template <int NQ, int NS>
 struct Bars {
-    uint64_t q_full, kv_full[NS], kv_empty[NS], s_full[NQ], s_free[NQ], p_ready[NQ], o_bar[NQ], o_done[NQ],
-        mma_final;
+    uint64_t q_full[2], q_empty[2], kv_full[NS], kv_empty[NS], s_full[NQ], s_free[NQ], p_ready[NQ], o_bar[NQ],
+        o_done[NQ], o_free[NQ], mma_final;
     uint32_t tmem_base;
     int abort;
 };
 
-// Causal prefill, one CTA = NQ*128 query rows of one (sequence, q-head).
-//   warpgroup 0: warp 0 lane 0 = TMA producer; warp 1 = TMEM owner, its lane 0 the MMA issuer
+// One work tile: NQ*128 query rows of one (sequence, q-head).  Tiles are numbered heaviest first
+// (the last query rows of a sequence attend to the most keys); CTA i takes tiles i, i + gridDim,
+// ... so every CTA gets a similar mix.
+template <int NQ, int BN_>
+struct TileInfo {
+    int b, h, g, q0, nkv, nq_live, qrow, kvrow0;
+    int nt[NQ];
+    __device__ __forceinline__ TileInfo(const TcParams &p, int t) {
+        const int ngroups = (p.ntok + NQ * BM - 1) / (NQ * BM);
+        const int per = p.nHead * p.nseq;
+        const int rank = t / per, rem = t - rank * per;
+        h = rem / p.nseq;
+        b = rem - h * p.nseq;
+        g = h / (p.nHead / p.nHeadKv);
+        q0 = (ngroups - 1 - rank) * NQ * BM;
+        nkv = 0;
+        nq_live = 0;
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+            const int start = q0 + q * BM;
+            nt[q] = start < p.ntok ? (min(start + BM, p.ntok) + BN_ - 1) / BN_ : 0;
+            nkv = max(nkv, nt[q]);
+            nq_live += nt[q] > 0;
+        }
+        qrow = (int)(((int64_t)b * p.nHead + h) * p.ntok + q0);
+        kvrow0 = (int)(p.kv_row_layer + (int64_t)b * p.kv_rows_per_slot + (int64_t)g * p.maxLen);
+    }
+};
+
+// Causal prefill, persistent: one CTA per SM walks work tiles (NQ*128 query rows of one
+// (sequence, q-head)) and keeps its TMEM, barriers and pipelines across them.
+//   warp 0: TMA (elected lane) -- Q of each tile into one of two Q buffers, K/V tiles into a ring
+//     that runs on across tiles, so the next tile's Q and first K/V arrive while this one ends;
+//   warp 1: TMEM owner and S issuer; warps 2, 3: P V issuers (query tile 0, 1);
 //   warpgroup 1+q: softmax of query tile q, thread = row = TMEM lane (warp w reaches TMEM lanes
-//   32*(w%4)..)
-// Per KV tile j and query tile q the MMA issuer runs S_q(j+1) = Q_q K_{j+1}^T as soon as group q
+//     32*(w%4)..).
+// Per KV tile j and query tile q the S issuer runs S_q(j+1) = Q_q K_{j+1}^T as soon as group q
 // has pulled S_q(j) into registers (s_free), and O_q += P_q(j) V_j once P_q(j) is in TMEM
-// (p_ready), so the tensor core works on one tile while the other groups' softmax runs.  A group
-// overwrites P_q and rescales O_q only after PV_q(j-1) has completed (o_bar).
+// (p_ready), so the tensor core works on one tile while the softmax runs.  A group overwrites
+// P_q and rescales O_q only after PV_q(j-1) has completed (o_bar); a tile's first P V (which
+// overwrites O_q) waits until the group has read out the previous tile's O_q (o_free).  Every
+// barrier phase comes from per-role running counts, not from the tile-local index.
 template <int NQ, int BN_>
 __global__ void __launch_bounds__(TcShape<NQ, BN_>::THREADS, 1)
 prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap vmap, const TcParams p) {
+    static_assert(NQ == 2, "one P V issuer warp per query tile: warps 2 and 3");
     using S_ = TcShape<NQ, BN_>;
+    using T_ = TileInfo<NQ, BN_>;
     constexpr int BNK = BN_;
     constexpr int NS = S_::NS;
     using B_ = Bars<NQ, NS>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-    uint8_t *sQ = base;                                  // [NQ] 16 KB tiles
-    uint8_t *sK = base + NQ * TILE_BYTES;                // [NS] tiles
+    uint8_t *sQ = base;                                  // [2 buffers][NQ] 16 KB tiles
+    uint8_t *sK = base + 2 * NQ * TILE_BYTES;            // [NS] tiles
     uint8_t *sV = sK + NS * S_::KV_TILE;                 // [NS] tiles
     B_ *bars = reinterpret_cast<B_ *>(sV + NS * S_::KV_TILE);
     volatile int *abort_flag = &bars->abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ngroups = (p.ntok + NQ * BM - 1) / (NQ * BM);
-    const int grp = ngroups - 1 - (int)blockIdx.x;  // heavy (late) tiles first
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int g = h / (p.nHead / p.nHeadKv);
-    const int q0 = grp * NQ * BM;
-    int nt[NQ];
-#pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-        const int start = q0 + q * BM;
-        nt[q] = start < p.ntok ? (min(start + BM, p.ntok) + BNK - 1) / BNK : 0;
-    }
-    int nkv = 0, nq_live = 0;
-#pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-        nkv = max(nkv, nt[q]);
-        nq_live += nt[q] > 0;
-    }
+    const int ntiles = ngroups * p.nHead * p.nseq;
 
     if (tid == 0) {
-        mbar_init(&bars->q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars->q_full[i], 1);
+            mbar_init(&bars->q_empty[i], 1);
+        }
         for (int i = 0; i < NS; ++i) {
             mbar_init(&bars->kv_full[i], 1);
             mbar_init(&bars->kv_empty[i], kIssuers);
@@ -365,6 +390,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             mbar_init(&bars->p_ready[q], BM);
             mbar_init(&bars->o_bar[q], 1);
             mbar_init(&bars->o_done[q], 1);
+            mbar_init(&bars->o_free[q], BM);
         }
         mbar_init(&bars->mma_final, kIssuers);
         bars->abort = 0;
@@ -378,8 +404,6 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    const int qrow = (int)(((int64_t)b * p.nHead + h) * p.ntok + q0);
-    const int kvrow0 = (int)(p.kv_row_layer + (int64_t)b * p.kv_rows_per_slot + (int64_t)g * p.maxLen);
 
     if (warp < 4) {
         setmaxnreg_dec<S_::REG_CTRL>();
@@ -390,24 +414,32 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         if (warp == 0) {
             // ---------------- TMA producer (one elected lane issues) ----------------
             const uint32_t leader = elect_one();
-            if (leader) mbar_arrive_expect_tx(&bars->q_full, nq_live * TILE_BYTES);
-            __syncwarp();
-#pragma unroll
-            for (int q = 0; q < NQ; ++q)
-                if (nt[q] > 0) tma_load_2d(sQ + q * TILE_BYTES, &qmap, 0, qrow + q * BM, &bars->q_full, leader);
-            int issued = 0;
-            for (int j = 0; j < nkv; ++j) {
-                const int st = j % NS;
-                if (!wait_all(&bars->kv_empty[st], ((j / NS) & 1) ^ 1, p.err, abort_flag)) break;
-                if (leader) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * S_::KV_TILE);
+            int it = 0, kvit = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+                const T_ ti(p, t);
+                const int qb = it & 1;
+                // Q buffer qb is free once the S MMAs of tile it-2 have completed
+                if (!wait_all(&bars->q_empty[qb], ((it >> 1) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
+                if (leader) mbar_arrive_expect_tx(&bars->q_full[qb], ti.nq_live * TILE_BYTES);
                 __syncwarp();
-                tma_load_2d(sK + st * S_::KV_TILE, &kmap, 0, kvrow0 + j * BNK, &bars->kv_full[st], leader);
-                tma_load_2d(sV + st * S_::KV_TILE, &vmap, 0, kvrow0 + j * BNK, &bars->kv_full[st], leader);
-                ++issued;
+#pragma unroll
+                for (int q = 0; q < NQ; ++q)
+                    if (ti.nt[q] > 0)
+                        tma_load_2d(sQ + (qb * NQ + q) * TILE_BYTES, &qmap, 0, ti.qrow + q * BM, &bars->q_full[qb], leader);
+                for (int j = 0; j < ti.nkv; ++j, ++kvit) {
+                    const int st = kvit % NS;
+                    if (!wait_all(&bars->kv_empty[st], ((kvit / NS) & 1) ^ 1, p.err, abort_flag)) { ok = false; break; }
+                    if (leader) mbar_arrive_expect_tx(&bars->kv_full[st], 2 * S_::KV_TILE);
+                    __syncwarp();
+                    tma_load_2d(sK + st * S_::KV_TILE, &kmap, 0, ti.kvrow0 + j * BNK, &bars->kv_full[st], leader);
+                    tma_load_2d(sV + st * S_::KV_TILE, &vmap, 0, ti.kvrow0 + j * BNK, &bars->kv_full[st], leader);
+                }
+                if (!ok) { ++it; break; }
             }
             // wait (bounded) until every copy issued into this CTA's shared memory has landed
-            wait_all(&bars->q_full, 0, nullptr, nullptr);
-            for (int j = max(0, issued - NS); j < issued; ++j)
+            for (int i = max(0, it - 2); i < it; ++i) wait_all(&bars->q_full[i & 1], (i >> 1) & 1, nullptr, nullptr);
+            for (int j = max(0, kvit - NS); j < kvit; ++j)
                 wait_all(&bars->kv_full[j % NS], (j / NS) & 1, nullptr, nullptr);
         } else if (warp == 1) {
             // ---------------- S issuer: S_q(j) = Q_q K_j^T ----------------
@@ -416,53 +448,72 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             // warps 2 and 3 issue O += P V.
             const uint32_t leader = elect_one();
             const uint32_t idesc_s = idesc_bf16(BNK, false);
-            bool ok = wait_all(&bars->q_full, 0, p.err, abort_flag);
-            for (int j = 0; j < nkv && ok; ++j) {
-                ok = wait_all(&bars->kv_full[j % NS], (j / NS) & 1, p.err, abort_flag);
-                if (!ok) break;
-                const uint32_t ka = smem_u32(sK + (j % NS) * S_::KV_TILE);
+            int it = 0, kvit = 0;
+            int ns[NQ] = {};
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+                const T_ ti(p, t);
+                const int qb = it & 1;
+                ok = wait_all(&bars->q_full[qb], (it >> 1) & 1, p.err, abort_flag);
+                for (int j = 0; j < ti.nkv && ok; ++j, ++kvit) {
+                    const int st = kvit % NS;
+                    ok = wait_all(&bars->kv_full[st], (kvit / NS) & 1, p.err, abort_flag);
+                    if (!ok) break;
+                    const uint32_t ka = smem_u32(sK + st * S_::KV_TILE);
 #pragma unroll
-                for (int q = 0; q < NQ; ++q) {
-                    if (!ok || j >= nt[q]) continue;
-                    // S_q(j-1) must be in the softmax group's registers before it is overwritten
-                    if (j > 0) ok = wait_all(&bars->s_free[q], (j - 1) & 1, p.err, abort_flag);
-                    if (!ok) continue;
-                    tc_fence_after();
-                    mma_s_k64(tmem + S_::col_s(q), sw128_desc(smem_u32(sQ + q * TILE_BYTES), 16), sw128_desc(ka, 16),
-                              idesc_s, leader);
-                    tc_commit(&bars->s_full[q], leader);
+                    for (int q = 0; q < NQ; ++q) {
+                        if (!ok || j >= ti.nt[q]) continue;
+                        // the previous S_q must be in the softmax group's registers before it is overwritten
+                        if (ns[q] > 0) ok = wait_all(&bars->s_free[q], (ns[q] - 1) & 1, p.err, abort_flag);
+                        if (!ok) continue;
+                        tc_fence_after();
+                        mma_s_k64(tmem + S_::col_s(q), sw128_desc(smem_u32(sQ + (qb * NQ + q) * TILE_BYTES), 16),
+                                  sw128_desc(ka, 16), idesc_s, leader);
+                        tc_commit(&bars->s_full[q], leader);
+                        ++ns[q];
+                    }
+                    tc_commit(&bars->kv_empty[st], leader);  // K_j is free once these S MMAs complete
                 }
-                tc_commit(&bars->kv_empty[j % NS], leader);  // K_j is free once these S MMAs complete
+                if (ok) tc_commit(&bars->q_empty[qb], leader);  // Q buffer free once this tile's S complete
             }
             // every MMA of the CTA has completed before TMEM can be released
             tc_commit(&bars->mma_final, leader);
             wait_all(&bars->mma_final, 0, p.err, nullptr);
         } else {
-            // ---------------- PV issuers: O_q += P_q(j) V_j for q = warp - 2, warp, ... ----------------
+            // ---------------- P V issuer for query tile q = warp - 2 ----------------
+            const int q = warp - 2;
             const uint32_t leader = elect_one();
             const uint32_t idesc_o = idesc_bf16(HD, true);
+            int kvit = 0, npv = 0, nto = 0;
             bool ok = true;
-            for (int j = 0; j < nkv && ok; ++j) {
-                // tile j's phase of kv_full has completed, so this warp's kv_empty arrival below
-                // belongs to tile j even when it issues nothing for it
-                ok = wait_all(&bars->kv_full[j % NS], (j / NS) & 1, p.err, abort_flag);
-                if (!ok) break;
-                const uint32_t va = smem_u32(sV + (j % NS) * S_::KV_TILE);
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const T_ ti(p, t);
+                const int ntq = q == 0 ? ti.nt[0] : ti.nt[1];
+                for (int j = 0; j < ti.nkv && ok; ++j, ++kvit) {
+                    // tile kvit's phase of kv_full has completed, so this warp's kv_empty arrival
+                    // belongs to it even when it issues nothing for it
+                    const int st = kvit % NS;
+                    ok = wait_all(&bars->kv_full[st], (kvit / NS) & 1, p.err, abort_flag);
+                    if (!ok) break;
+                    if (j < ntq) {
+                        // the tile's first P V overwrites O_q: the group has read the previous tile's out
+                        if (j == 0 && nto > 0) ok = wait_all(&bars->o_free[q], (nto - 1) & 1, p.err, abort_flag);
+                        if (ok) ok = wait_all(&bars->p_ready[q], npv & 1, p.err, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t va = smem_u32(sV + st * S_::KV_TILE);
 #pragma unroll
-                for (int q = 0; q < NQ; ++q) {
-                    if (!ok || (q & 1) != warp - 2 || j >= nt[q]) continue;
-                    ok = wait_all(&bars->p_ready[q], j & 1, p.err, abort_flag);
-                    if (!ok) continue;
-                    tc_fence_after();
-#pragma unroll
-                    for (int kb = 0; kb < BNK / 64; ++kb)
-                        mma_pv_k64(tmem + S_::col_o(q), tmem + S_::col_p(q) + kb * 32,
-                                   sw128_desc(va + kb * 4 * 2048, S_::KV_TILE), idesc_o, (j > 0 || kb > 0) ? 1u : 0u,
-                                   leader);
-                    tc_commit(&bars->o_bar[q], leader);
-                    if (j == nt[q] - 1) tc_commit(&bars->o_done[q], leader);
+                        for (int kb = 0; kb < BNK / 64; ++kb)
+                            mma_pv_k64(tmem + S_::col_o(q), tmem + S_::col_p(q) + kb * 32,
+                                       sw128_desc(va + kb * 4 * 2048, S_::KV_TILE), idesc_o,
+                                       (j > 0 || kb > 0) ? 1u : 0u, leader);
+                        tc_commit(&bars->o_bar[q], leader);
+                        if (j == ntq - 1) tc_commit(&bars->o_done[q], leader);
+                        ++npv;
+                    }
+                    tc_commit(&bars->kv_empty[st], leader);  // V_j is free once these P V MMAs complete
                 }
-                tc_commit(&bars->kv_empty[j % NS], leader);  // V_j is free once these PV MMAs complete
+                if (ntq > 0) ++nto;
             }
             tc_commit(&bars->mma_final, leader);
         }
@@ -471,95 +522,106 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
         // ---------------- softmax of query tile q ----------------
         const int q = (warp - 4) >> 2;
         const int r = (warp & 3) * 32 + lane;
-        const int row = q0 + q * BM + r;
-        const int row_first = q0 + q * BM;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const float C = kLog2e / 8.0f;  // log2(e) / sqrt(64)
-        float m_run = -INFINITY, l = 0.f;
+        int ns = 0, npv = 0, nto = 0;
         bool ok = true;
-        for (int j = 0; j < nt[q] && ok; ++j) {
-            // warp-uniform verdict: the TMEM loads below are warp-collective
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], j & 1, p.err, abort_flag));
-            if (!ok) break;
-            tc_fence_after();
-            uint32_t sr[BNK];
-#pragma unroll
-            for (int c = 0; c < BNK / 32; ++c) {
-                uint32_t *rr = sr + 32 * c;
-                TL_LD32(tmem + lane_base + S_::col_s(q) + 32 * c, rr);
-            }
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
-            const int k0 = j * BNK;
-            if (k0 + BNK - 1 > row_first || k0 + BNK > p.ntok) {  // tile crosses the diagonal or the end
-#pragma unroll
-                for (int c = 0; c < BNK; ++c)
-                    if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
-            }
-            // row maximum: four independent chains of three-input max
-            float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int c = 0; c < BNK; c += 8) {
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    mq[u] = max3f(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
-            }
-            const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
-            const float ms = mx * C;
-            const bool grow = ms > m_run + kRescaleThreshold || m_run == -INFINITY;
-            float alpha = 1.f;
-            if (grow) {
-                alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - ms);
-                m_run = ms;
-                l *= alpha;
-            }
-            if (j > 0) {
-                // PV_q(j-1) must be complete before P_q is overwritten (and before O_q is rescaled)
-                ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_bar[q], (j - 1) & 1, p.err, abort_flag));
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            const T_ ti(p, t);
+            const int ntq = q == 0 ? ti.nt[0] : ti.nt[1];
+            if (ntq == 0) continue;
+            const int row_first = ti.q0 + q * BM;
+            const int row = row_first + r;
+            float m_run = -INFINITY, l = 0.f;
+            for (int j = 0; j < ntq && ok; ++j) {
+                // warp-uniform verdict: the TMEM loads below are warp-collective
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars->s_full[q], ns & 1, p.err, abort_flag));
                 if (!ok) break;
+                ++ns;
                 tc_fence_after();
-            }
-            if (__any_sync(0xffffffffu, grow && j > 0)) {
-                // O_q holds the sum through tile j-1: rescale it in TMEM, 16 columns at a time
+                uint32_t sr[BNK];
 #pragma unroll
-                for (int c = 0; c < HD / 16; ++c) {
-                    uint32_t orr[16];
-                    TL_LD16(tmem + lane_base + S_::col_o(q) + 16 * c, orr);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-                    TL_ST16(tmem + lane_base + S_::col_o(q) + 16 * c, orr);
+                for (int c = 0; c < BNK / 32; ++c) {
+                    uint32_t *rr = sr + 32 * c;
+                    TL_LD32(tmem + lane_base + S_::col_s(q) + 32 * c, rr);
                 }
-            }
-            // p = 2^(s*C - m): the argument in packed pairs, the sum in four packed accumulators
-            const float2 c2 = make_float2(C, C), n2 = make_float2(-m_run, -m_run);
-            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                             make_float2(0.f, 0.f)};
-            uint32_t pk[BNK / 2];
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
+                const int k0 = j * BNK;
+                if (k0 + BNK - 1 > row_first || k0 + BNK > p.ntok) {  // tile crosses the diagonal or the end
 #pragma unroll
-            for (int c = 0; c < BNK; c += 2) {
-                const float2 x = ffma2(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2, n2);
-                const float2 pp = (kPolyMod > 0 && (c >> 1) % (kPolyMod > 0 ? kPolyMod : 1) == (kPolyMod > 0 ? kPolyMod : 1) - 1)
-                                      ? exp2_poly2(x)
-                                      : make_float2(ex2(x.x), ex2(x.y));
-                acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pp);
-                pk[c / 2] = pack_bf16(pp.x, pp.y);
-            }
-            const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
-            const float2 a = fadd2(a01, a23);
-            l += a.x + a.y;
+                    for (int c = 0; c < BNK; ++c)
+                        if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
+                }
+                // row maximum: four independent chains of three-input max
+                float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < BNK / 64; ++c) {
-                uint32_t *rr = pk + 32 * c;
-                TL_ST32(tmem + lane_base + S_::col_p(q) + 32 * c, rr);
+                for (int c = 0; c < BNK; c += 8) {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        mq[u] = max3f(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+                }
+                const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
+                const float ms = mx * C;
+                const bool grow = ms > m_run + kRescaleThreshold || m_run == -INFINITY;
+                float alpha = 1.f;
+                if (grow) {
+                    alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - ms);
+                    m_run = ms;
+                    l *= alpha;
+                }
+                if (j > 0) {
+                    // PV_q(j-1) must be complete before P_q is overwritten (and before O_q is
+                    // rescaled); at j == 0 the previous tile's last P V has completed (o_done)
+                    ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_bar[q], (npv - 1) & 1, p.err, abort_flag));
+                    if (!ok) break;
+                    tc_fence_after();
+                }
+                if (__any_sync(0xffffffffu, grow && j > 0)) {
+                    // O_q holds the sum through tile j-1: rescale it in TMEM, 16 columns at a time
+#pragma unroll
+                    for (int c = 0; c < HD / 16; ++c) {
+                        uint32_t orr[16];
+                        TL_LD16(tmem + lane_base + S_::col_o(q) + 16 * c, orr);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+                        TL_ST16(tmem + lane_base + S_::col_o(q) + 16 * c, orr);
+                    }
+                }
+                // p = 2^(s*C - m): the argument in packed pairs, the sum in four packed accumulators
+                const float2 c2 = make_float2(C, C), n2 = make_float2(-m_run, -m_run);
+                float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                 make_float2(0.f, 0.f)};
+                uint32_t pk[BNK / 2];
+#pragma unroll
+                for (int c = 0; c < BNK; c += 2) {
+                    const float2 x = ffma2(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), c2, n2);
+                    const float2 pp = (kPolyMod > 0 && (c >> 1) % (kPolyMod > 0 ? kPolyMod : 1) == (kPolyMod > 0 ? kPolyMod : 1) - 1)
+                                          ? exp2_poly2(x)
+                                          : make_float2(ex2(x.x), ex2(x.y));
+                    acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pp);
+                    pk[c / 2] = pack_bf16(pp.x, pp.y);
+                }
+                const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
+                const float2 a = fadd2(a01, a23);
+                l += a.x + a.y;
+#pragma unroll
+                for (int c = 0; c < BNK / 64; ++c) {
+                    uint32_t *rr = pk + 32 * c;
+                    TL_ST32(tmem + lane_base + S_::col_p(q) + 32 * c, rr);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&bars->p_ready[q]);
+                ++npv;
             }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&bars->p_ready[q]);
-        }
-        if (ok && nt[q] > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], 0, p.err, abort_flag));
-        if (ok && nt[q] > 0) {
+            if (!ok) break;
+            // epilogue: O_q out of TMEM (then it may be overwritten by the next tile), normalise, store
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_done[q], nto & 1, p.err, abort_flag));
+            if (!ok) break;
+            ++nto;
             tc_fence_after();
             uint32_t orr[HD];
 #pragma unroll
@@ -568,19 +630,22 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 TL_LD32(tmem + lane_base + S_::col_o(q) + 32 * c, rr);
             }
             tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&bars->o_free[q]);
             if (row < p.ntok) {
                 const float inv = l > 0.f ? 1.f / l : 0.f;
                 float *dst = p.out.ptr;
 #pragma unroll
                 for (int i = 0; i < HD; i += 4) {
-                    const int64_t o = p.out.at(b, row, h, i);
+                    const int64_t o = p.out.at(ti.b, row, ti.h, i);
                     if (p.out.sd == 1 && (o & 3) == 0) {
                         *reinterpret_cast<float4 *>(dst + o) =
                             make_float4(__uint_as_float(orr[i]) * inv, __uint_as_float(orr[i + 1]) * inv,
                                         __uint_as_float(orr[i + 2]) * inv, __uint_as_float(orr[i + 3]) * inv);
                     } else {
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) dst[p.out.at(b, row, h, i + u)] = __uint_as_float(orr[i + u]) * inv;
+                        for (int u = 0; u < 4; ++u)
+                            dst[p.out.at(ti.b, row, ti.h, i + u)] = __uint_as_float(orr[i + u]) * inv;
                     }
                 }
             }
@@ -651,26 +716,27 @@ cudaError_t launch_shape(const PrefillArgs &a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         smem_set[dev & 63] = smem;
     }
-    dim3 grid((a.ntok + NQ * BM - 1) / (NQ * BM), a.nHead, a.nseq);
+    // persistent: one CTA per SM (TMEM and shared memory allow one), at most one per tile
+    static int sms[64] = {};
+    if (sms[dev & 63] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev & 63] = n > 0 ? n : 1;
+    }
+    const long long ntiles = (long long)((a.ntok + NQ * BM - 1) / (NQ * BM)) * a.nHead * a.nseq;
+    if (ntiles > INT32_MAX) return cudaErrorNotSupported;
+    const int grid = (int)std::min<long long>(ntiles, sms[dev & 63]);
     kern<<<grid, S_::THREADS, smem, s>>>(qm, km, vm, p);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-#ifndef TL_PREFILL_NQ
-#define TL_PREFILL_NQ 2
-#endif
-
 cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s) {
     if (a.headDim != HD || a.kv.dtype != TL_KV_BF16 || a.qb == nullptr || a.pos0 != nullptr ||
         a.kf.ptr != nullptr)
         return cudaErrorNotSupported;
-#if TL_PREFILL_NQ == 3
-    return launch_shape<3, 64>(a, s);
-#else
     return launch_shape<2, 128>(a, s);
-#endif
 }
 
 }  // namespace tl
