@@ -433,17 +433,18 @@ def run_prefill(args, dist):
         ms, core_ms, pro_ms, flops = prefill_point(S, max(5, args.steps // 2), args.warmup, dist)
         tf = flops / (ms / 1e3) / 1e12
         tf_core = flops / (core_ms / 1e3) / 1e12 if core_ms > 0 else None
+        peak = pk["bf16_tflops"] * dist.world  # whole job: N GPUs
         res[str(S)] = {"ms_per_step": round(ms, 4), "tflops": round(tf, 1),
-                       "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4), "flops": flops,
+                       "frac_of_bf16_peak": round(tf / peak, 4), "flops": flops,
                        "attention_core": {"ms": round(core_ms, 4),
                                           "tflops": None if tf_core is None else round(tf_core, 1),
                                           "frac_of_bf16_peak": None if tf_core is None else
-                                          round(tf_core / pk["bf16_tflops"], 4)},
+                                          round(tf_core / peak, 4)},
                        "prologue_ms": round(pro_ms, 4)}
     return {"workload": "causal prefill, 8 sequences (sharded over the GPUs), 32 q / 8 kv heads, head_dim 64, "
                         "bf16 KV (tcgen05); step = RoPE + cache write + attention (end to end on the device); "
                         "attention_core = the attention kernel alone (CUPTI device time)",
-            "n_gpus": dist.world, "by_seq_len": res, "peak_tflops": pk["bf16_tflops"], "peak_src": pk["src"]}
+            "n_gpus": dist.world, "by_seq_len": res, "peak_tflops_per_gpu": pk["bf16_tflops"], "peak_src": pk["src"]}
 
 
 # ------------------------------------------------------------- TinyLlama decode latency
