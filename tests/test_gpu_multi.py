@@ -1,9 +1,10 @@
-"""Split-KV decode across two GPUs (tl_decode_attention_dist: the decode kernel stores each
-(sequence, head) result into every rank's buffer over NVLink and merges after a bounded flag
-wait) against the single-GPU decode over the whole context, on two B200s.  One process per GPU,
-spawned; the NCCL id (used once, to exchange the IPC handles) is created in the parent.  Three
-calls in a row with different queries exercise both halves of the double-buffered exchange and
-the epoch flags."""
+"""Split-KV decode across 2, 4 and 8 GPUs (tl_decode_attention_dist: the decode kernel stores each
+(sequence, head) result into every rank's buffer over NVLink as epoch-tagged words and merges them
+as they arrive) against the single-GPU decode over the whole context, on B200s; each count runs
+when the box has that many GPUs.  One process per GPU, spawned; the NCCL id (used once, to
+exchange the IPC handles) is created in the parent.  Three calls in a row with different
+queries exercise both halves of the double-buffered exchange and the epoch tags, and with 4 or 8
+ranks the shorter sequence leaves the last ranks' slices empty."""
 import ctypes as C
 import multiprocessing as mp
 import os
@@ -32,7 +33,7 @@ def _worker(rank, nranks, uid, kvd, L, out_q):
     k = rng.standard_normal((B, L, Hkv * D), dtype=np.float32)
     v = rng.standard_normal((B, L, Hkv * D), dtype=np.float32)
     qs = [rng.standard_normal((B, Hq * D), dtype=np.float32) for _ in range(3)]
-    lens = [L - 1, L // 2 - 3]  # the second sequence ends inside rank 0's slice
+    lens = [L - 1, L // 2 - 3]  # the second sequence ends in the first half of the ranks' slices
     p = lambda t: C.c_void_p(t.data_ptr())
     h = C.c_void_p()
     _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, 500000.0, sl, B, kvd, rank))
@@ -74,10 +75,11 @@ def _worker(rank, nranks, uid, kvd, L, out_q):
         _lib.lib.tl_attn_destroy(h)
 
 
+@pytest.mark.parametrize("nranks", [2, 4, 8])
 @pytest.mark.parametrize("kvd", [0, 1])
-def test_splitkv_two_gpus_matches_one(cuda_lib, kvd):
-    if _ngpus() < 2:
-        pytest.skip("needs two GPUs")
+def test_splitkv_gpus_match_one(cuda_lib, kvd, nranks):
+    if _ngpus() < nranks:
+        pytest.skip(f"needs {nranks} GPUs")
     _lib = cuda_lib
     uid = C.create_string_buffer(128)
     _lib.check(_lib.lib.tl_dist_unique_id(uid))
@@ -85,12 +87,12 @@ def test_splitkv_two_gpus_matches_one(cuda_lib, kvd):
     q = ctx.Queue()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     os.environ.update(env)
-    procs = [ctx.Process(target=_worker, args=(r, 2, uid.raw, kvd, 8192, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, nranks, uid.raw, kvd, 8192, q)) for r in range(nranks)]
     for pr in procs:
         pr.start()
     results = {}
     try:
-        for _ in range(2):
+        for _ in range(nranks):
             rank, got, ref, err = q.get(timeout=180)
             assert err is None, (rank, err)
             results[rank] = (got, ref)
@@ -100,6 +102,6 @@ def test_splitkv_two_gpus_matches_one(cuda_lib, kvd):
             if pr.is_alive():
                 pr.kill()
     refs = results[0][1]
-    for rank in (0, 1):
+    for rank in range(nranks):
         for i, (got, ref) in enumerate(zip(results[rank][0], refs)):
             assert np.allclose(got, ref, rtol=1e-4, atol=1e-5), (rank, i, float(np.max(np.abs(got - ref))))
