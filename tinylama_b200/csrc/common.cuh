@@ -19,6 +19,13 @@
 
 namespace tl {
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialisation may
+// start while the previous kernel on its stream still runs; it must wait here before it reads
+// anything that kernel writes.  A kernel that others depend on signals early that they may be
+// scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

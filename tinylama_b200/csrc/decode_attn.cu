@@ -132,6 +132,8 @@ decode_kernel(const DecodeArgs a) {
         *abort_flag = 0;
         fence_mbar_init();
     }
+    // launched behind the RoPE/append kernel: positions, q and the cache are read after it
+    pdl_wait();
     if (warp == 0) build_schedule(a, prefix, lens, max_nch, lane, err);
     __syncthreads();
     const int total_units = prefix[a.nseq] * a.nHeadKv;
@@ -153,8 +155,9 @@ decode_kernel(const DecodeArgs a) {
             bool ok = true;
             int qs = 0, u = 0;
             uint32_t qp = 0;
+            bool first = true;
             while (ok) {
-                if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, err, abort_flag)) { ok = false; break; }
+                if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, first, err, abort_flag)) { ok = false; break; }
                 if (u < 0) break;
                 const Unit un = decode_unit(a, prefix, lens, u);
                 const int64_t row0 = a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
@@ -362,8 +365,7 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         cur = smem;
     }
-    kern<<<num_ctas, C::THREADS, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(num_ctas), dim3(C::THREADS), smem, s, a);
 }
 
 template <typename KV, int D>

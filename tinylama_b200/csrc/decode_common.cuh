@@ -104,9 +104,12 @@ __device__ __forceinline__ int unit_of_rank(const DecodeArgs &a, const int *pref
 // Producer (one thread): claim the next unit and publish it; -1 when none remain.  Returns
 // false if the wait for a free queue slot gave up (abort or timeout).
 __device__ __forceinline__ bool unitq_push(const DecodeArgs &a, UnitQueue *q, const int *prefix, int total_units,
-                                           int &slot, uint32_t &phase, int &u, unsigned *err,
+                                           int &slot, uint32_t &phase, int &u, bool &first, unsigned *err,
                                            volatile int *abort_flag) {
-    const int k = (int)atomicAdd(a.work, 1u);
+    // a CTA's first unit is its own rank (no round trip before the first copies); later ones
+    // come from the counter, past the ranks the grid took that way
+    const int k = first ? (int)blockIdx.x : (int)(gridDim.x + atomicAdd(a.work, 1u));
+    first = false;
     u = k < total_units ? unit_of_rank(a, prefix, k) : -1;
     if (!mbar_wait(&q->empty[slot], phase ^ 1u, err, abort_flag)) return false;
     q->id[slot] = u;

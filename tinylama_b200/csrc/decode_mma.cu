@@ -180,6 +180,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
         *abort_flag = 0;
         fence_mbar_init();
     }
+    // launched behind the RoPE/append kernel: positions, q and the cache are read after it
+    pdl_wait();
     if (warp == 0) build_schedule(a, prefix, lens, max_nch, lane, err);
     __syncthreads();
     const int total_units = prefix[a.nseq] * a.nHeadKv;
@@ -199,8 +201,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             bool ok = true;
             int qs = 0, u = 0;
             uint32_t qp = 0;
+            bool first = true;
             while (ok) {
-                if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, err, abort_flag)) { ok = false; break; }
+                if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, first, err, abort_flag)) { ok = false; break; }
                 if (u < 0) break;
                 const Unit un = decode_unit(a, prefix, lens, u);
                 const int row0 = (int)a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
@@ -475,8 +478,7 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         cur = smem;
     }
-    kern<<<num_ctas, C::THREADS, smem, s>>>(km, vm, a);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(num_ctas), dim3(C::THREADS), smem, s, km, vm, a);
 }
 
 template <typename KV, int D, int G>

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/tl_attn.h"
@@ -88,6 +89,27 @@ struct tl_attn {
 };
 
 namespace tl {
+
+// Launch a kernel with programmatic stream serialisation: its CTAs may be scheduled while the
+// previous kernel on the stream still runs, and it waits (pdl_wait) before reading that
+// kernel's output.  Used for the decode kernels, which follow the RoPE/append launch in a
+// decode step.  (The persistent prefill kernel is launched normally: its CTAs, resident early,
+// would take the SMs' shared memory from the RoPE kernel still running.)
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ---- launchers (return cudaError_t of the launch) -----------------------------------------
 // RoPE on q and/or k plus optional append of (rotated k, v) into the cache.

@@ -61,6 +61,7 @@ constexpr int kHeadsPerThread = 8;
 // (the angle depends only on the position and the pair).  Segment B appends v.
 template <typename KV>
 __global__ void rope_append_kernel(const RopeAppendArgs a, const RopeTab tab) {
+    pdl_launch_dependents();  // a decode kernel launched behind this one may be scheduled
     const int half = a.headDim / 2;
     const int hq = a.rope_q ? a.nHead : 0;
     const int hk = (a.rope_k || a.store) ? a.nHeadKv : 0;
@@ -156,6 +157,7 @@ __global__ void rope_append_kernel(const RopeAppendArgs a, const RopeTab tab) {
 // bit-identical to the generic kernel.
 template <typename KV, int D4T>
 __global__ void __launch_bounds__(256) rope_append_tok_kernel(const RopeAppendArgs a, const RopeTab tab) {
+    pdl_launch_dependents();  // a decode kernel launched behind this one may be scheduled
     __shared__ float2 cs[kMaxRopePairs];
     const int D = a.headDim;
     const int D4 = D4T > 0 ? D4T : D / 4;
@@ -232,6 +234,7 @@ __global__ void __launch_bounds__(256) rope_append_tok_kernel(const RopeAppendAr
 // stores.
 template <typename KV, int D4T>
 __global__ void __launch_bounds__(256) rope_append_pos_kernel(const RopeAppendArgs a, const RopeTab tab) {
+    pdl_launch_dependents();  // a decode kernel launched behind this one may be scheduled
     __shared__ float2 cs[kMaxRopePairs];
     const int D = a.headDim;
     const int D4 = D4T > 0 ? D4T : D / 4;
