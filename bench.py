@@ -84,6 +84,10 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a moment to start: begin the timed region once it is sampling
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except (OSError, FileNotFoundError):
             self.proc = None
 
@@ -610,8 +614,7 @@ def run_reference(args, dist):
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * B / value, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "batched multi-sequence decode (TinyLlama GQA attention)" if gqa else
-                               "batched multi-sequence decode (Llama-2-7B-style attention)",
+        "config": {"workload": "batched multi-sequence decode (Llama-2-7B-style attention)",
                    "seqs_per_gpu": B, "ctx_len": "U[256,4096] seeded", "n_head": Hq, "n_head_kv": Hkv,
                    "head_dim": D, "kv_dtype": "f32"},
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
@@ -624,7 +627,7 @@ def run_reference(args, dist):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_batched",
