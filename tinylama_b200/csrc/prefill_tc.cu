@@ -5,20 +5,21 @@
 // Inputs are bf16 (Q staged by the RoPE kernel, K/V from the cache the same launch sequence
 // appended to), products accumulate in fp32 in tensor memory, softmax runs in fp32.
 //
-// One CTA owns NQ x 128 query rows (NQ = 2: two tiles of 128) of one (sequence, q-head).  A TMA
-// warp brings Q once and K/V tiles of BN = 128 positions (2-D tensor maps, 128-byte swizzle, no
-// multicast) into a three-deep ring.  tcgen05.mma issue is spread over three warps of the control
-// warpgroup, each a converged warp with one elected lane issuing: one issues S_q = Q_q K^T
-// (4 x kind::f16, M=128, N=128, K=16, A and B K-major from shared memory), two issue O_q += P_q V
-// (A = P from TMEM, B = V MN-major from shared memory).  Issuing an MMA occupies the issuing
-// warp's scheduler partition, and spreading it keeps the four softmax warps of a group in step.
-// NQ softmax warpgroups (thread = query row = TMEM lane) load S, mask causally, keep the online
-// max/sum in fp32 (log2 domain), write P as packed bf16 into TMEM and rescale O in TMEM only
-// when a row's maximum grows past 2^8.  One pair in four of the exponentials runs as a
-// polynomial on the FMA pipe, the rest on MUFU.  S and P have separate TMEM columns, so
-// S_q(j+1) runs on the tensor core while the softmax of S_q(j) is still in flight.  KV tiles
-// past the diagonal are skipped.  Every mbarrier wait is bounded (common.cuh); TMEM is released
-// on every exit path after all issued MMAs have completed.
+// Persistent: one CTA per SM walks work tiles of NQ x 128 query rows (NQ = 2) of one (sequence,
+// q-head), heaviest first, keeping its TMEM and pipelines across tiles.  A TMA warp brings each
+// tile's Q into one of two buffers and K/V tiles of BN = 128 positions (2-D tensor maps, 128-byte
+// swizzle, no multicast) into a three-deep ring that runs on across tiles.  tcgen05.mma issue is
+// spread over three warps of the control warpgroup, each a converged warp with one elected lane
+// issuing: one issues S_q = Q_q K^T (4 x kind::f16, M=128, N=128, K=16, A and B K-major from
+// shared memory), two issue O_q += P_q V (A = P from TMEM, B = V MN-major from shared memory).
+// Issuing an MMA occupies the issuing warp's scheduler partition, and spreading it keeps the four
+// softmax warps of a group in step.  NQ softmax warpgroups (thread = query row = TMEM lane) load
+// S, mask causally, keep the online max/sum in fp32 (log2 domain), write P as packed bf16 into
+// TMEM and rescale O in TMEM only when a row's maximum grows past 2^8.  One pair in four of the
+// exponentials runs as a polynomial on the FMA pipe, the rest on MUFU.  S and P have separate
+// TMEM columns, so S_q(j+1) runs on the tensor core while the softmax of S_q(j) is still in
+// flight.  KV tiles past the diagonal are skipped.  Every mbarrier wait is bounded (common.cuh);
+// TMEM is released on every exit path after all issued MMAs have completed.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -211,9 +212,9 @@ struct TcShape {
     static constexpr int THREADS = 128 * (NQ + 1);
     static constexpr int KV_TILE = BN_ * HD * 2;                      // bytes of one K or V tile
     static constexpr int NS = (96 * 1024) / (2 * KV_TILE);            // K/V ring depth: 96 KB
-    static constexpr int REG_LAUNCH = (65536 / THREADS) / 8 * 8;       // 168 (NQ=2) / 128 (NQ=3)
-    static constexpr int REG_CTRL = NQ == 2 ? 104 : 80;
-    static constexpr int REG_SOFT = NQ == 2 ? 200 : 144;
+    static constexpr int REG_LAUNCH = (65536 / THREADS) / 8 * 8;       // 168 for 384 threads
+    static constexpr int REG_CTRL = 104;
+    static constexpr int REG_SOFT = 200;
     static_assert(REG_CTRL + NQ * REG_SOFT <= (NQ + 1) * REG_LAUNCH, "register split exceeds the launch allotment");
     static constexpr int COL_P0 = NQ * BN_;
     static constexpr int COL_O0 = COL_P0 + NQ * BN_ / 2;
