@@ -217,3 +217,55 @@ def test_dist_single_rank_matches_local(env, exchange):
         os.environ.pop("TL_DIST_NCCL", None)
         if old is not None:
             os.environ["TL_DIST_NCCL"] = old
+
+
+@pytest.mark.parametrize("kvd,Hq,Hkv,D,lens", [
+    (0, 32, 4, 64, [2048]),           # TinyLlama batch 1: 8 CTAs of 256 positions per kv head
+    (0, 32, 4, 64, [1]),
+    (0, 32, 4, 64, [1, 100, 700]),    # chunks past a short sequence's end are empty
+    (1, 32, 4, 64, [2048]),
+    (1, 32, 8, 128, [1000, 3]),
+    (0, 32, 8, 128, [4000]),
+    (1, 8, 8, 64, [70, 511]),
+])
+def test_decode_cluster_mode_matches_queue_mode(env, kvd, Hq, Hkv, D, lens):
+    """Few short sequences run in cluster mode (one thread-block cluster per (sequence,
+    kv-head), merged through distributed shared memory); TL_DECODE_CLUSTER=0 sends the same
+    call through the unit queue and the global merge.  Both against the oracle and each other."""
+    torch, _lib = env
+    rng = np.random.default_rng(sum(lens) * 3 + kvd)
+    base = 10000.0
+    B = len(lens)
+    h = create(_lib, 1, Hq, Hkv, D, max(lens) + 1, B, kvd, base)
+    old = os.environ.pop("TL_DECODE_CLUSTER", None)
+    try:
+        caches = fill_cache(torch, _lib, h, 0, lens, Hkv, D, rng, base, kvd)
+        q = randn(rng, B, Hq * D)
+        pos = np.array([L - 1 for L in lens], np.int32)
+        dq = torch.from_numpy(q).cuda()
+        dpos = torch.from_numpy(pos).cuda()
+        f = pos.ctypes.data_as(C.c_void_p)
+        outs = []
+        for mode in ("1", "0"):
+            os.environ["TL_DECODE_CLUSTER"] = mode
+            o = torch.empty(B, Hq * D, device="cuda")
+            for _ in range(2):  # a second call reuses the barriers and counters
+                _lib.check(_lib.lib.tl_decode_attention(h, 0, 0, B, ptr(dpos), f, ptr(dq), ptr(o), None))
+            _lib.check(_lib.lib.tl_check_device(h, None))
+            outs.append(o.cpu().numpy())
+        for b, L in enumerate(lens):
+            kc, vc = caches[b]
+            qb = q[b].reshape(-1, 1)
+            ref = ora.attention_cached(qb, kc, vc, L, Hq, Hkv, D)
+            exact = numpy_ref.attention(qb, kc, vc, Hq, Hkv, D, np.array([L - 1]), L) if L >= 1024 else None
+            for got in outs:
+                err, allowed = parity(got[b].reshape(-1, 1), ref, exact, TOL_F32 if kvd == 0 else TOL_BF16)
+                assert err <= allowed, (b, L, err, allowed)
+        # the two modes sum in a different order (chunk boundaries, merge tree): f32 results
+        # agree to the f32 bound, bf16 ones (same hi/lo rounding of q and p) to 1e-3
+        assert max_rel_err(outs[0], outs[1]) < (TOL_F32 if kvd == 0 else 1e-3)
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+        os.environ.pop("TL_DECODE_CLUSTER", None)
+        if old is not None:
+            os.environ["TL_DECODE_CLUSTER"] = old

@@ -398,6 +398,7 @@ cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
         const cudaError_t e = launch_decode_mma(a, num_ctas, s);
         if (e != cudaErrorNotSupported) return e;
     }
+    if (a.cluster > 0) return cudaErrorNotSupported;  // cluster mode exists only in the tensor-core kernel
     if (a.headDim == 64) {
         return a.kv.dtype == TL_KV_F32 ? launch_g<float, 64>(a, num_ctas, s)
                                        : launch_g<__nv_bfloat16, 64>(a, num_ctas, s);

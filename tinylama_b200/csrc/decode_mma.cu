@@ -76,7 +76,8 @@ struct MmaCfg {
     static constexpr int OFF_WL = OFF_WM + NW * G * 4;
     static constexpr int OFF_WO = OFF_WL + NW * G * 4;
     static constexpr int OFF_CW = OFF_WO + NW * G * D * 4;
-    static constexpr int OFF_PREFIX = OFF_CW + kMaxChunksPerSeq * G * 4;
+    static constexpr int OFF_CX = OFF_CW + kMaxChunksPerSeq * G * 4;   // cluster mode: 2 mbarriers,
+    static constexpr int OFF_PREFIX = OFF_CX + 16 + G * (D + 2) * 4;    // then (m, l, o) of this CTA
     static size_t smem_bytes(int nseq) { return 1024 + (size_t)OFF_PREFIX + 4 * (2 * (size_t)nseq + 1) + 16; }
 };
 
@@ -145,7 +146,135 @@ __device__ __forceinline__ uint32_t swz(uint32_t box, int row, int chunk) {
     return box + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
-template <typename KV, int D, int G>
+// ---- cluster mode: one cluster of CL CTAs per (sequence, kv-head), merged in shared memory ----
+constexpr int kMaxCluster = 8;  // portable cluster size
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// address of the same shared-memory location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// bounded wait with cluster-scope acquire (the arrivals came from other CTAs of the cluster)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *err,
+                                                  volatile int *abort_flag) {
+    auto test = [&]() {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        return ok != 0;
+    };
+    if (test()) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (test()) return true;
+        if (abort_flag && *abort_flag) return false;
+        if (globaltimer_ns() - t0 > TL_WAIT_NS) {
+            if (err) atomicOr(err, TL_DEVERR_TIMEOUT);
+            if (abort_flag) *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+// End of the unit in cluster mode (the NW*32 consumer threads): this CTA's (m, l, o) for the G
+// heads go to its own shared memory; the CL-1 other CTAs then arrive on rank 0's barrier, rank 0
+// reads their values through distributed shared memory, merges
+//   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L
+// into out, and releases each of them (their shared memory must stay until it has read it).
+// Every wait is bounded, and every CTA arrives whatever its own state, so none waits for ever.
+template <int G, int D, int NW>
+__device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit &un, const float *wm, const float *wl,
+                                                 const float *wo, uint64_t *clb, float *cx, int tid,
+                                                 volatile int *abort_flag) {
+    named_bar(1, NW * 32);
+    float *cm = cx, *cl = cx + G, *co = cx + 2 * G;
+    for (int e = tid; e < G * D; e += NW * 32) {
+        const int h = e / D, dd = e - h * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * G + h]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float sw = safe_exp2_diff(wm[w * G + h], M);
+            L = fmaf(wl[w * G + h], sw, L);
+            O = fmaf(wo[(w * G + h) * D + dd], sw, O);
+        }
+        co[e] = O;
+        if (dd == 0) { cm[h] = M; cl[h] = L; }
+    }
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+    named_bar(1, NW * 32);
+    const uint32_t CL = cluster_size(), rank = cluster_rank();
+    if (CL == 1) {
+        for (int e = tid; e < G * D; e += NW * 32) {
+            const int h = e / D, dd = e - h * D;
+            a.out[((int64_t)un.b * a.nHead + un.g * G + h) * D + dd] = cl[h] > 0.f ? co[e] / cl[h] : 0.f;
+        }
+        return;
+    }
+    if (rank != 0) {
+        if (tid == 0) mbar_arrive_remote(cluster_addr(&clb[0], 0));
+        // not cut short by this CTA's own abort: rank 0 may still be reading this shared memory
+        __all_sync(0xffffffffu, mbar_wait_cluster(&clb[1], 0, a.err, nullptr));
+        return;
+    }
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_cluster(&clb[0], 0, a.err, abort_flag));
+    if (ok) {
+        for (int e = tid; e < G * D; e += NW * 32) {
+            const int h = e / D, dd = e - h * D;
+            float m[kMaxCluster], l[kMaxCluster], o[kMaxCluster];
+            float M = -INFINITY;
+#pragma unroll
+            for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r) {
+                if (r >= CL) break;
+                m[r] = ld_cluster(cluster_addr(&cm[h], r));
+                l[r] = ld_cluster(cluster_addr(&cl[h], r));
+                o[r] = ld_cluster(cluster_addr(&co[e], r));
+                M = fmaxf(M, m[r]);
+            }
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r) {
+                if (r >= CL) break;
+                const float w = safe_exp2_diff(m[r], M);
+                L = fmaf(l[r], w, L);
+                O = fmaf(o[r], w, O);
+            }
+            a.out[((int64_t)un.b * a.nHead + un.g * G + h) * D + dd] = (L > 0.f) ? O / L : 0.f;
+        }
+    }
+    named_bar(1, NW * 32);  // rank 0 has read every CTA's values
+    if (tid >= 1 && tid < (int)CL) mbar_arrive_remote(cluster_addr(&clb[1], (uint32_t)tid));
+}
+
+template <typename KV, int D, int G, bool CLU>
 __global__ void __launch_bounds__(MmaCfg<KV, D, G>::THREADS, MmaCfg<KV, D, G>::MIN_CTAS)
 decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const DecodeArgs a) {
@@ -165,6 +294,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     int *prefix = reinterpret_cast<int *>(smem + C::OFF_PREFIX);
     int *lens = prefix + (a.nseq + 1);
     UnitQueue *uq = reinterpret_cast<UnitQueue *>(smem + C::OFF_UQ);
+    uint64_t *clb = reinterpret_cast<uint64_t *>(smem + C::OFF_CX);  // cluster mode: [0] gather, [1] release
+    float *cx = reinterpret_cast<float *>(smem + C::OFF_CX + 16);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned *err = a.err;
@@ -177,18 +308,41 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             mbar_init(&uq->full[s], 1);
             mbar_init(&uq->empty[s], C::NW);
         }
+        if constexpr (CLU) {
+            const int cl = (int)cluster_size();
+            mbar_init(&clb[0], cl > 1 ? cl - 1 : 1);  // the other CTAs of the cluster
+            mbar_init(&clb[1], 1);                    // rank 0, done reading
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
+    // cluster mode: every CTA's barriers exist before any CTA arrives on them
+    if constexpr (CLU) cluster_sync_all();
     // launched behind the RoPE/append kernel: positions, q and the cache are read after it
     pdl_wait();
-    if (warp == 0) build_schedule(a, prefix, lens, max_nch, lane, err);
-    __syncthreads();
-    const int total_units = prefix[a.nseq] * a.nHeadKv;
-    if (max_nch[0] > kMaxChunksPerSeq ||
-        (max_nch[0] > 1 && decode_partial_floats_dev(total_units, G, D) > a.partial_cap)) {
-        if (tid == 0) atomicOr(err, TL_DEVERR_BAD_ARG);
-        return;
+    int total_units = 0;
+    Unit cu{};
+    if constexpr (!CLU) {
+        if (warp == 0) build_schedule(a, prefix, lens, max_nch, lane, err);
+        __syncthreads();
+        total_units = prefix[a.nseq] * a.nHeadKv;
+        if (max_nch[0] > kMaxChunksPerSeq ||
+            (max_nch[0] > 1 && decode_partial_floats_dev(total_units, G, D) > a.partial_cap)) {
+            if (tid == 0) atomicOr(err, TL_DEVERR_BAD_ARG);
+            return;
+        }
+    } else {
+        // this CTA's unit: chunk `rank` of (sequence, kv-head) `cluster index`
+        __syncthreads();
+        const int cl = (int)cluster_size(), rank = (int)cluster_rank();
+        const int pair = (int)blockIdx.x / cl;
+        cu.b = pair / a.nHeadKv;
+        cu.g = pair - cu.b * a.nHeadKv;
+        cu.c = rank;
+        cu.nch = cl;
+        cu.n = local_len(a, cu.b, err);
+        cu.p0 = min(rank * a.chunk, cu.n);
+        cu.p1 = min(cu.p0 + a.chunk, cu.n);
     }
 
     if (warp == C::NW) {
@@ -199,13 +353,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             uint32_t phase = 0;
             long issued = 0;
             bool ok = true;
-            int qs = 0, u = 0;
-            uint32_t qp = 0;
-            bool first = true;
-            while (ok) {
-                if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, first, err, abort_flag)) { ok = false; break; }
-                if (u < 0) break;
-                const Unit un = decode_unit(a, prefix, lens, u);
+            // the copies of one unit's tiles into the ring
+            auto issue_unit = [&](const Unit &un) {
                 const int row0 = (int)a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
                 for (int p = un.p0; p < un.p1; p += C::T) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, err, abort_flag)) { ok = false; break; }
@@ -220,8 +369,20 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                     ++issued;
                     if (++stage == C::NS) { stage = 0; phase ^= 1u; }
                 }
+            };
+            if constexpr (CLU) {
+                issue_unit(cu);
+            } else {
+                int qs = 0, u = 0;
+                uint32_t qp = 0;
+                bool first = true;
+                while (ok) {
+                    if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, first, err, abort_flag)) { ok = false; break; }
+                    if (u < 0) break;
+                    issue_unit(decode_unit(a, prefix, lens, u));
+                }
             }
-            if (ok) unitq_finish(a);
+            if (!CLU && ok) unitq_finish(a);
             // wait (bounded) for every copy issued into this CTA's shared memory
             const int outstanding = issued < (long)C::NS ? (int)issued : C::NS;
             int s = stage;
@@ -242,10 +403,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     uint32_t phase = 0;
     int qs = 0;
     uint32_t qp = 0;
-    while (true) {
-        const int u = unitq_pop(uq, qs, qp, err, abort_flag, lane);
-        if (u < 0) break;
-        const Unit un = decode_unit(a, prefix, lens, u);
+    // one unit: q fragments, the tile loop, then this warp's (m, l, o) into wm/wl/wo
+    auto consume_unit = [&](const Unit &un) -> bool {
         // q fragments (A rows = heads of this kv group; rows >= G are zero): bf16 hi + lo for
         // bf16 caches; tf32 big + small of the four columns of one chunk per k16 block for f32
         uint32_t qh[C::KT][C::F32 ? 4 : 2], ql[C::KT][C::F32 ? 4 : 2];
@@ -422,6 +581,18 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                 }
             }
         }
+        return ok;
+    };
+    if constexpr (CLU) {
+        consume_unit(cu);
+        cluster_epilogue<G, D, C::NW>(a, cu, wm, wl, wo, clb, cx, tid, abort_flag);
+        return;
+    }
+    while (true) {
+        const int u = unitq_pop(uq, qs, qp, err, abort_flag, lane);
+        if (u < 0) break;
+        const Unit un = decode_unit(a, prefix, lens, u);
+        const bool ok = consume_unit(un);
         unit_epilogue<G, D, C::NW>(a, un, u, prefix, wm, wl, wo, cw, is_last_flag, tid, warp, lane);
         if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
     }
@@ -467,17 +638,30 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     if (!make_cache_map(&km, a.kv.k, rows, D, C::F32) || !make_cache_map(&vm, a.kv.v, rows, D, C::F32))
         return cudaErrorNotSupported;
     const size_t smem = C::smem_bytes(a.nseq);
-    auto kern = decode_mma_kernel<KV, D, G>;
-    // only when it grows (per device): steady-state launches make no attribute calls
-    static size_t smem_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    size_t &cur = smem_set[dev & 63];
-    if (smem > cur) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // only when it grows (per device and kernel): steady-state launches make no attribute calls
+    auto ensure_smem = [&](auto kern, size_t *set) -> cudaError_t {
+        size_t &cur = set[dev & 63];
+        if (smem > cur) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            cur = smem;
+        }
+        return cudaSuccess;
+    };
+    if (a.cluster > 0) {
+        if (a.cluster > kMaxCluster || num_ctas % a.cluster != 0) return cudaErrorInvalidValue;
+        static size_t smem_set_clu[64] = {};
+        auto kern = decode_mma_kernel<KV, D, G, true>;
+        cudaError_t e = ensure_smem(kern, smem_set_clu);
         if (e != cudaSuccess) return e;
-        cur = smem;
+        return launch_pdl_cluster(kern, dim3(num_ctas), dim3(C::THREADS), smem, a.cluster, s, km, vm, a);
     }
+    static size_t smem_set[64] = {};
+    auto kern = decode_mma_kernel<KV, D, G, false>;
+    cudaError_t e = ensure_smem(kern, smem_set);
+    if (e != cudaSuccess) return e;
     return launch_pdl(kern, dim3(num_ctas), dim3(C::THREADS), smem, s, km, vm, a);
 }
 
@@ -486,8 +670,9 @@ int occ_t() {
     using C = MmaCfg<KV, D, G>;
     int n = 0;
     const size_t smem = C::smem_bytes(256);
-    cudaFuncSetAttribute(decode_mma_kernel<KV, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mma_kernel<KV, D, G>, C::THREADS, smem) != cudaSuccess)
+    auto kern = decode_mma_kernel<KV, D, G, false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, C::THREADS, smem) != cudaSuccess)
         n = 1;
     return n < 1 ? 1 : n;
 }

@@ -111,6 +111,27 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// The same, with thread-block clusters of `cluster` CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster,
+                               cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // ---- launchers (return cudaError_t of the launch) -----------------------------------------
 // RoPE on q and/or k plus optional append of (rotated k, v) into the cache.
 //   positions: token t of sequence b sits at position pos0[b] + t (pos0 on the device, or
@@ -142,6 +163,8 @@ struct DecodeArgs {
     int layer, slot0;
     int pos_offset;        // cache position of index 0 of this shard (split-KV across GPUs)
     int chunk;             // positions per work unit (multiple of 32)
+    int cluster;           // > 0: one thread-block cluster of this many CTAs per (sequence,
+                           // kv-head), one chunk each, merged through distributed shared memory
     KvLayout kv;
     float *partial;        // scratch
     size_t partial_cap;    // floats

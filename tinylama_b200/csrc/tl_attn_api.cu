@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -140,9 +141,38 @@ cudaStream_t pick(const tl_attn *h, void *stream) {
 struct Plan {
     int chunk, ctas;
     size_t partial_floats;
+    int cluster;  // > 0: cluster mode (one cluster of this many CTAs per (sequence, kv-head))
 };
 
-Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset, int slice) {
+// Cluster mode serves few, short sequences (batch-1 decode): one thread-block cluster of up to
+// 8 CTAs per (sequence, kv-head), one chunk of at most 512 positions per CTA, merged through
+// distributed shared memory -- no schedule, no unit queue, no global partials.  Used when all
+// the clusters fit on the GPU at once.  TL_DECODE_CLUSTER=0 in the environment of a call turns
+// it off (read on every call).
+bool cluster_mode_allowed() {
+    const char *e = getenv("TL_DECODE_CLUSTER");
+    return !(e && e[0] == '0');
+}
+
+bool plan_cluster(const tl_attn *h, int nseq, int nmax, int ctas, Plan *p) {
+    const int G = h->nHead / h->nHeadKv;
+    if (!cluster_mode_allowed() || !decode_mma_covers(h->headDim, G, h->kvDtype)) return false;
+    constexpr int kTarget = 256, kMaxChunk = 512, kMaxCl = 8, kTile = 64;
+    const int cl = std::max(1, std::min(kMaxCl, (nmax + kTarget - 1) / kTarget));
+    int chunk = (nmax + cl - 1) / cl;
+    chunk = std::max(kTile, (chunk + kTile - 1) / kTile * kTile);
+    if (chunk > kMaxChunk) return false;
+    const long long grid = (long long)nseq * h->nHeadKv * cl;
+    if (grid > ctas) return false;
+    p->chunk = chunk;
+    p->ctas = (int)grid;
+    p->partial_floats = 0;
+    p->cluster = cl;
+    return true;
+}
+
+Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset, int slice,
+                 bool cluster_ok = false) {
     const int G = h->nHead / h->nHeadKv;
     const int occ = decode_ctas_per_sm(h->headDim, G, h->kvDtype);
     const int ctas = h->numSms * occ;
@@ -159,6 +189,8 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
         tot += n;
         nmax = std::max(nmax, n);
     }
+    Plan p{};
+    if (cluster_ok && plan_cluster(h, nseq, nmax, ctas, &p)) return p;
     long long want = (tot * h->nHeadKv + (long long)ctas * 4 - 1) / ((long long)ctas * 4);
     int chunk = (int)std::min<long long>(1024, std::max<long long>(32, want));
     chunk = (chunk + 31) / 32 * 32;
@@ -172,7 +204,6 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
         multi |= nch > 1;
         units += (long long)nch * h->nHeadKv;
     }
-    Plan p;
     p.chunk = chunk;
     p.ctas = (int)std::max<long long>(1, std::min<long long>(units, ctas));
     p.partial_floats = multi ? decode_partial_floats((int)units, G, h->headDim) : 0;
@@ -182,7 +213,8 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
 int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, const int *pos_host,
                const float *q, float *out, cudaStream_t s, int pos_offset, float *lse_out,
                const DecodeArgs::Peer *px = nullptr) {
-    Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen);
+    // cluster mode writes the output directly: not for partial (lse) or cross-GPU results
+    Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen, !px && !lse_out);
     TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
     DecodeArgs a{};
     a.q = q;
@@ -204,7 +236,18 @@ int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, c
     a.err = h->dErr;
     a.lse_out = lse_out;
     if (px) a.px = *px;
+    a.cluster = p.cluster;
     cudaError_t e = launch_decode(a, p.ctas, s);
+    if (e == cudaErrorNotSupported && p.cluster > 0) {
+        // the tensor-core kernel could not be set up: plan again for the CUDA-core kernel
+        p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen);
+        TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
+        a.chunk = p.chunk;
+        a.partial = h->dPartial;
+        a.partial_cap = h->partialCap;
+        a.cluster = 0;
+        e = launch_decode(a, p.ctas, s);
+    }
     if (e == cudaErrorNotSupported) return fail(TL_ERR_UNSUPPORTED, "decode: shape not covered");
     TL_CUDA(e);
     return TL_OK;
