@@ -133,7 +133,9 @@ TL_API int tl_prefill_layer_host(tl_attn *h, int layer, int slot, const float *q
                           const float *v, int seqLen, float *ctx);
 /* Batched decode step with host buffers (the host-tier form of tl_decode_step): q
  * [nseq][nHead*headDim], k, v [nseq][nHeadKv*headDim], pos [nseq], out like q, all host
- * memory (pinned memory makes the copies asynchronous).  Synchronous. */
+ * memory (pinned memory makes the copies asynchronous).  Synchronous.  A large batch (>= 0.3
+ * GB of K/V) is cut into 2-4 parts of consecutive sequences: the copies of one part overlap
+ * the attention of another (environment TL_HOST_PARTS=1..4 sets the number of parts). */
 TL_API int tl_decode_batch_host(tl_attn *h, int layer, int slot0, int nseq, const int *pos,
                          const float *q, const float *k, const float *v, float *out);
 

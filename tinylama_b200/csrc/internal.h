@@ -75,6 +75,10 @@ struct tl_attn {
     void *dQb = nullptr;
     size_t qbCap = 0;               // bytes
     cudaStream_t stream = nullptr;  // the handle's own stream (host tier)
+    // host-tier batched decode: copy streams (in, out) and per-part events, so that the copies
+    // of one part of the batch overlap the attention of another
+    cudaStream_t cpIn = nullptr, cpOut = nullptr;
+    cudaEvent_t evIn[4] = {}, evOut[4] = {}, evDone = nullptr;
     // multi-GPU split-KV
     void *comm = nullptr;           // ncclComm_t (used to exchange the IPC handles)
     int nranks = 1, rank = 0;

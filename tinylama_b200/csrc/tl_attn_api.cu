@@ -322,6 +322,86 @@ int prefill_attention(tl_attn *h, int layer, int slot0, int nseq, int S, HeadVie
 
 bool tc_prefill_eligible(const tl_attn *h) { return h->kvDtype == TL_KV_BF16 && h->headDim == 64; }
 
+int ensure_copy_streams(tl_attn *h) {
+    if (h->cpIn) return TL_OK;
+    TL_CUDA(cudaStreamCreateWithFlags(&h->cpOut, cudaStreamNonBlocking));
+    for (int j = 0; j < 4; ++j) {
+        TL_CUDA(cudaEventCreateWithFlags(&h->evIn[j], cudaEventDisableTiming));
+        TL_CUDA(cudaEventCreateWithFlags(&h->evOut[j], cudaEventDisableTiming));
+    }
+    TL_CUDA(cudaEventCreateWithFlags(&h->evDone, cudaEventDisableTiming));
+    TL_CUDA(cudaStreamCreateWithFlags(&h->cpIn, cudaStreamNonBlocking));  // last: marks the set complete
+    return TL_OK;
+}
+
+// Split a batch into `parts` runs of consecutive sequences with about equal KV bytes (the
+// attention time of a part follows its K/V bytes).  cut[j] .. cut[j+1] is part j.
+int split_by_kv(const int *pos, int nseq, int parts, int *cut) {
+    long long tot = 0;
+    for (int b = 0; b < nseq; ++b) tot += pos[b] + 1;
+    int j = 1;
+    long long acc = 0;
+    cut[0] = 0;
+    for (int b = 0; b < nseq && j < parts; ++b) {
+        acc += pos[b] + 1;
+        if (acc * parts >= tot * j) cut[j++] = b + 1;
+    }
+    while (j < parts) cut[j++] = nseq;
+    cut[parts] = nseq;
+    // drop empty parts
+    int n = 0;
+    for (int i = 0; i < parts; ++i)
+        if (cut[i + 1] > cut[i]) cut[++n] = cut[i + 1];
+    return n;
+}
+
+// The copies and launches of tl_decode_batch_host; on an error return, work may still be
+// queued on the three streams.
+int decode_batch_host_impl(tl_attn *h, int layer, int slot0, int nseq, const int *pos, const float *q,
+                           const float *k, const float *v, float *out, long long kv_rows) {
+    const int Dq = h->nHead * h->headDim, Dk = h->nHeadKv * h->headDim;
+    const size_t nq = (size_t)nseq * Dq, nk = (size_t)nseq * Dk;
+    TL_TRY(ensure_io(h, 2 * nq + 2 * nk));
+    TL_TRY(ensure_copy_streams(h));
+    float *dq = h->dIo, *dk = dq + nq, *dv = dk + nk, *dout = dv + nk;
+    // Parts: the batch is cut into up to 4 runs of sequences; the copies in of part j+1 and out
+    // of part j-1 (one copy stream each way) overlap the attention of part j on the handle's
+    // stream.  Few K/V bytes (attention shorter than ~50 us at HBM speed) keep one part: there
+    // the extra launches would cost more than the overlap saves.
+    const double kv_bytes = (double)kv_rows * Dk * 2 * (h->kvDtype == TL_KV_F32 ? 4 : 2);
+    int parts = kv_bytes >= 1.2e9 ? 4 : kv_bytes >= 3e8 ? 2 : 1;
+    if (const char *e = getenv("TL_HOST_PARTS")) parts = std::max(1, std::min(4, atoi(e)));  // override
+    parts = std::min(parts, nseq);
+    int cut[5];
+    parts = split_by_kv(pos, nseq, parts, cut);
+    // the in-stream starts after whatever the handle's stream has queued (the cache writes)
+    TL_CUDA(cudaEventRecord(h->evDone, h->stream));
+    TL_CUDA(cudaStreamWaitEvent(h->cpIn, h->evDone, 0));
+    TL_CUDA(cudaMemcpyAsync(h->dPos, pos, sizeof(int) * nseq, cudaMemcpyHostToDevice, h->cpIn));
+    for (int j = 0; j < parts; ++j) {
+        const size_t b0 = cut[j], nb = cut[j + 1] - cut[j];
+        TL_CUDA(cudaMemcpyAsync(dq + b0 * Dq, q + b0 * Dq, nb * Dq * 4, cudaMemcpyHostToDevice, h->cpIn));
+        TL_CUDA(cudaMemcpyAsync(dk + b0 * Dk, k + b0 * Dk, nb * Dk * 4, cudaMemcpyHostToDevice, h->cpIn));
+        TL_CUDA(cudaMemcpyAsync(dv + b0 * Dk, v + b0 * Dk, nb * Dk * 4, cudaMemcpyHostToDevice, h->cpIn));
+        TL_CUDA(cudaEventRecord(h->evIn[j], h->cpIn));
+    }
+    for (int j = 0; j < parts; ++j) {
+        const int b0 = cut[j], nb = cut[j + 1] - cut[j];
+        TL_CUDA(cudaStreamWaitEvent(h->stream, h->evIn[j], 0));
+        TL_TRY(tl_decode_step(h, layer, slot0 + b0, nb, h->dPos + b0, pos + b0, dq + (size_t)b0 * Dq,
+                              dk + (size_t)b0 * Dk, dv + (size_t)b0 * Dk, dout + (size_t)b0 * Dq, h->stream));
+        TL_CUDA(cudaEventRecord(h->evOut[j], h->stream));
+    }
+    for (int j = 0; j < parts; ++j) {
+        const size_t b0 = cut[j], nb = cut[j + 1] - cut[j];
+        TL_CUDA(cudaStreamWaitEvent(h->cpOut, h->evOut[j], 0));
+        TL_CUDA(cudaMemcpyAsync(out + b0 * Dq, dout + b0 * Dq, nb * Dq * 4, cudaMemcpyDeviceToHost, h->cpOut));
+    }
+    TL_CUDA(cudaEventRecord(h->evDone, h->cpOut));
+    TL_CUDA(cudaStreamWaitEvent(h->stream, h->evDone, 0));
+    return TL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -413,6 +493,13 @@ void tl_attn_destroy(tl_attn *h) {
     cudaFree(h->dQb);
     cudaFree(h->dGather);
     if (h->hPinned) cudaFreeHost(h->hPinned);
+    for (int j = 0; j < 4; ++j) {
+        if (h->evIn[j]) cudaEventDestroy(h->evIn[j]);
+        if (h->evOut[j]) cudaEventDestroy(h->evOut[j]);
+    }
+    if (h->evDone) cudaEventDestroy(h->evDone);
+    if (h->cpIn) cudaStreamDestroy(h->cpIn);
+    if (h->cpOut) cudaStreamDestroy(h->cpOut);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
 }
@@ -650,20 +737,21 @@ int tl_decode_batch_host(tl_attn *h, int layer, int slot0, int nseq, const int *
                          const float *q, const float *k, const float *v, float *out) {
     if (!h || !pos || !q || !k || !v || !out) return fail(TL_ERR_INVALID, "NULL argument");
     TL_TRY(check_layer_slot(h, layer, slot0, nseq));
+    long long kv_rows = 0;
     for (int b = 0; b < nseq; ++b) {
         if (pos[b] >= h->maxLen) return fail(TL_ERR_KV_FULL, "KV cache full");
         if (pos[b] < 0) return fail(TL_ERR_INVALID, "negative position");
+        kv_rows += pos[b] + 1;
     }
     DeviceGuard g(h->device);
-    const size_t nq = (size_t)nseq * h->nHead * h->headDim, nk = (size_t)nseq * h->nHeadKv * h->headDim;
-    TL_TRY(ensure_io(h, 2 * nq + 2 * nk));
-    float *dq = h->dIo, *dk = dq + nq, *dv = dk + nk, *dout = dv + nk;
-    TL_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
-    TL_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
-    TL_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
-    TL_CUDA(cudaMemcpyAsync(h->dPos, pos, sizeof(int) * nseq, cudaMemcpyHostToDevice, h->stream));
-    TL_TRY(tl_decode_step(h, layer, slot0, nseq, h->dPos, pos, dq, dk, dv, dout, h->stream));
-    TL_CUDA(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    const int rc = decode_batch_host_impl(h, layer, slot0, nseq, pos, q, k, v, out, kv_rows);
+    if (rc != TL_OK) {
+        // what was queued may still read the caller's buffers: wait for it
+        if (h->cpIn) cudaStreamSynchronize(h->cpIn);
+        cudaStreamSynchronize(h->stream);
+        if (h->cpOut) cudaStreamSynchronize(h->cpOut);
+        return rc;
+    }
     return finish(h, h->stream);
 }
 
