@@ -192,18 +192,22 @@ def test_prefill_step_batched(env, kvd, S):
         _lib.lib.tl_attn_destroy(h)
 
 
+@pytest.mark.parametrize("cluster", ["1", "0"])
 @pytest.mark.parametrize("exchange", ["peer", "nccl"])
-def test_dist_single_rank_matches_local(env, exchange):
+def test_dist_single_rank_matches_local(env, exchange, cluster):
     """tl_decode_attention_dist with one rank must reproduce the single-GPU result.  "peer" is
     the fused exchange (the decode kernel stores its (o, m, l) into the gather buffer, raises
     the epoch flag, waits for it and merges); "nccl" is the fallback (local partials, NCCL
     all-gather, merge launch), chosen by TL_DIST_NCCL=1 at tl_dist_init.  Three calls in a row
-    use both halves of the exchange buffer."""
+    use both halves of the exchange buffer.  TL_DECODE_CLUSTER=0 keeps the decode kernel off
+    cluster mode (one cluster per (sequence, kv-head), which these sizes otherwise select)."""
     torch, _lib = env
     rng = np.random.default_rng(31)
     lens = [3000, 129, 1]
     B, Hq, Hkv, D = 3, 32, 8, 128
     old = os.environ.pop("TL_DIST_NCCL", None)
+    old_cl = os.environ.pop("TL_DECODE_CLUSTER", None)
+    os.environ["TL_DECODE_CLUSTER"] = cluster
     if exchange == "nccl":
         os.environ["TL_DIST_NCCL"] = "1"
     h = create(_lib, 1, Hq, Hkv, D, 4096, B, 1, 500000.0)
@@ -228,6 +232,9 @@ def test_dist_single_rank_matches_local(env, exchange):
         os.environ.pop("TL_DIST_NCCL", None)
         if old is not None:
             os.environ["TL_DIST_NCCL"] = old
+        os.environ.pop("TL_DECODE_CLUSTER", None)
+        if old_cl is not None:
+            os.environ["TL_DECODE_CLUSTER"] = old_cl
 
 
 @pytest.mark.parametrize("kvd,Hq,Hkv,D,lens", [

@@ -75,9 +75,13 @@ def _worker(rank, nranks, uid, kvd, L, out_q):
         _lib.lib.tl_attn_destroy(h)
 
 
+@pytest.mark.parametrize("cluster", ["1", "0"])
 @pytest.mark.parametrize("nranks", [2, 4, 8])
 @pytest.mark.parametrize("kvd", [0, 1])
-def test_splitkv_gpus_match_one(cuda_lib, kvd, nranks):
+def test_splitkv_gpus_match_one(cuda_lib, kvd, nranks, cluster):
+    """Split-KV over nranks GPUs against the whole context on one.  At these sizes the decode
+    kernel runs in cluster mode (one cluster per (sequence, kv-head)); TL_DECODE_CLUSTER=0
+    runs the unit queue instead."""
     if _ngpus() < nranks:
         pytest.skip(f"needs {nranks} GPUs")
     _lib = cuda_lib
@@ -85,11 +89,19 @@ def test_splitkv_gpus_match_one(cuda_lib, kvd, nranks):
     _lib.check(_lib.lib.tl_dist_unique_id(uid))
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    os.environ.update(env)
+    # spawned children take the parent's environment: set it for them, then put it back
+    saved = {k: os.environ.get(k) for k in ("NCCL_NVLS_ENABLE", "TL_DECODE_CLUSTER")}
+    os.environ.update(NCCL_NVLS_ENABLE="0", TL_DECODE_CLUSTER=cluster)
     procs = [ctx.Process(target=_worker, args=(r, nranks, uid.raw, kvd, 8192, q)) for r in range(nranks)]
-    for pr in procs:
-        pr.start()
+    try:
+        for pr in procs:
+            pr.start()
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
     results = {}
     try:
         for _ in range(nranks):

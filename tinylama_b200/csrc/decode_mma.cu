@@ -202,6 +202,21 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     }
 }
 
+// The merged (O, M, L) of one head element: ctx = O / L, or (O, M, L) to the (o, lse) output,
+// or to every rank's exchange buffer (split-KV across GPUs).
+template <int D>
+__device__ __forceinline__ void cluster_final(const DecodeArgs &a, int b, int head, int dd, float O, float M, float L) {
+    if (a.px.nranks > 0) {
+        peer_store_final<D>(a, b, head, dd, O, M, L);
+    } else if (a.lse_out != nullptr) {
+        float *dst = a.lse_out + ((int64_t)b * a.nHead + head) * (D + 2);
+        dst[dd] = O;
+        if (dd == 0) { dst[D] = M; dst[D + 1] = L; }
+    } else {
+        a.out[((int64_t)b * a.nHead + head) * D + dd] = (L > 0.f) ? O / L : 0.f;
+    }
+}
+
 // End of the unit in cluster mode (the NW*32 consumer threads): this CTA's (m, l, o) for the G
 // heads go to its own shared memory; the CL-1 other CTAs then arrive on rank 0's barrier, rank 0
 // reads their values through distributed shared memory, merges
@@ -235,7 +250,7 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
     if (CL == 1) {
         for (int e = tid; e < G * D; e += NW * 32) {
             const int h = e / D, dd = e - h * D;
-            a.out[((int64_t)un.b * a.nHead + un.g * G + h) * D + dd] = cl[h] > 0.f ? co[e] / cl[h] : 0.f;
+            cluster_final<D>(a, un.b, un.g * G + h, dd, co[e], cm[h], cl[h]);
         }
         return;
     }
@@ -267,7 +282,7 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
                 L = fmaf(l[r], w, L);
                 O = fmaf(o[r], w, O);
             }
-            a.out[((int64_t)un.b * a.nHead + un.g * G + h) * D + dd] = (L > 0.f) ? O / L : 0.f;
+            cluster_final<D>(a, un.b, un.g * G + h, dd, O, M, L);
         }
     }
     named_bar(1, NW * 32);  // rank 0 has read every CTA's values
@@ -586,18 +601,20 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     if constexpr (CLU) {
         consume_unit(cu);
         cluster_epilogue<G, D, C::NW>(a, cu, wm, wl, wo, clb, cx, tid, abort_flag);
-        return;
+        // split-KV across GPUs: CTA i merges pair i (every cluster is resident: the host checks)
+        if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);
+    } else {
+        while (true) {
+            const int u = unitq_pop(uq, qs, qp, err, abort_flag, lane);
+            if (u < 0) break;
+            const Unit un = decode_unit(a, prefix, lens, u);
+            const bool ok = consume_unit(un);
+            unit_epilogue<G, D, C::NW>(a, un, u, prefix, wm, wl, wo, cw, is_last_flag, tid, warp, lane);
+            if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
+        }
+        // split-KV across GPUs: this CTA's share of the cross-rank merges, after its own units
+        if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);
     }
-    while (true) {
-        const int u = unitq_pop(uq, qs, qp, err, abort_flag, lane);
-        if (u < 0) break;
-        const Unit un = decode_unit(a, prefix, lens, u);
-        const bool ok = consume_unit(un);
-        unit_epilogue<G, D, C::NW>(a, un, u, prefix, wm, wl, wo, cw, is_last_flag, tid, warp, lane);
-        if (named_bar_or(1, C::NW * 32, (!ok) || (*abort_flag != 0))) break;
-    }
-    // split-KV across GPUs: this CTA's share of the cross-rank merges, after its own units
-    if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -713,6 +730,67 @@ cudaError_t launch_decode_mma(const DecodeArgs &a, int num_ctas, cudaStream_t s)
 #undef TL_MMA_CASE
 #undef TL_MMA_CASE_F32
     return cudaErrorNotSupported;
+}
+
+namespace {
+template <typename KV, int D, int G>
+int cluster_capacity_t(int cluster) {
+    using C = MmaCfg<KV, D, G>;
+    const size_t smem = C::smem_bytes(512);  // at least what a cluster-mode launch uses (nseq <= 512)
+    auto kern = decode_mma_kernel<KV, D, G, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(cluster);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+}  // namespace
+
+int decode_mma_cluster_capacity(int headDim, int group, int dtype, int cluster) {
+    if (!decode_mma_covers(headDim, group, dtype) || cluster < 1 || cluster > kMaxCluster) return 0;
+    // cached per (device, dtype, head_dim, group, cluster size)
+    static int cache[16][2][2][4][kMaxCluster + 1];
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int gi = group == 1 ? 0 : group == 2 ? 1 : group == 4 ? 2 : 3;
+    const int di = dtype == TL_KV_F32 ? 0 : 1, hi = headDim == 64 ? 0 : 1;
+    if (dev < 0 || dev >= 16) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    int &c = cache[dev][di][hi][gi][cluster];
+    if (c > 0) return c;
+    int n = 0;
+#define TL_CAP(KV, DD)                                               \
+    switch (group) {                                                 \
+        case 1: n = cluster_capacity_t<KV, DD, 1>(cluster); break;   \
+        case 2: n = cluster_capacity_t<KV, DD, 2>(cluster); break;   \
+        case 4: n = cluster_capacity_t<KV, DD, 4>(cluster); break;   \
+        case 8: n = cluster_capacity_t<KV, DD, 8>(cluster); break;   \
+    }
+    if (dtype == TL_KV_F32) {
+        if (headDim == 64) n = group == 8 ? cluster_capacity_t<float, 64, 8>(cluster) : cluster_capacity_t<float, 64, 4>(cluster);
+        else n = group == 8 ? cluster_capacity_t<float, 128, 8>(cluster) : cluster_capacity_t<float, 128, 4>(cluster);
+    } else if (headDim == 64) {
+        TL_CAP(__nv_bfloat16, 64)
+    } else {
+        TL_CAP(__nv_bfloat16, 128)
+    }
+#undef TL_CAP
+    c = n;
+    return n;
 }
 
 int decode_mma_ctas_per_sm(int headDim, int group, int dtype) {

@@ -196,6 +196,9 @@ int decode_ctas_per_sm(int headDim, int group, int dtype);
 bool decode_mma_covers(int headDim, int group, int dtype);
 cudaError_t launch_decode_mma(const DecodeArgs &a, int num_ctas, cudaStream_t s);
 int decode_mma_ctas_per_sm(int headDim, int group, int dtype);
+// Clusters of `cluster` CTAs of the tensor-core decode kernel that can be resident at once
+// (cudaOccupancyMaxActiveClusters; 0 if the query fails).
+int decode_mma_cluster_capacity(int headDim, int group, int dtype, int cluster);
 size_t decode_partial_floats(int total_units, int group, int headDim);
 
 // Merge G per-rank (o, m, l) partials [G][nseq][nHead][d+2] into out [nseq][nHead][d].

@@ -144,27 +144,37 @@ struct Plan {
     int cluster;  // > 0: cluster mode (one cluster of this many CTAs per (sequence, kv-head))
 };
 
-// Cluster mode serves few, short sequences (batch-1 decode): one thread-block cluster of up to
-// 8 CTAs per (sequence, kv-head), one chunk of at most 512 positions per CTA, merged through
-// distributed shared memory -- no schedule, no unit queue, no global partials.  Used when all
-// the clusters fit on the GPU at once.  TL_DECODE_CLUSTER=0 in the environment of a call turns
-// it off (read on every call).
+// Cluster mode: one thread-block cluster of up to 8 CTAs per (sequence, kv-head), CTA r of a
+// cluster taking chunk r, merged through distributed shared memory -- no schedule, no unit
+// queue, no global partials.  It needs every cluster resident at once (grid <= the resident
+// CTAs) and is chosen for
+//   * few short sequences (chunks of at most 512 positions: batch-1 decode, latency-bound), or
+//   * sequences of about equal length (mean >= 3/4 of the longest) whose clusters fill at least
+//     3/4 of the resident CTAs: every CTA then streams the same share, and there is no tail of
+//     unevenly finished units or chunk merge to wait for.
+// With the cross-GPU exchange the clusters must also be co-resident by the occupancy API's
+// count, since every CTA waits for the other ranks' values of its pair after its own chunk.
+// TL_DECODE_CLUSTER=0 in the environment of a call turns cluster mode off (read on every call).
 bool cluster_mode_allowed() {
     const char *e = getenv("TL_DECODE_CLUSTER");
     return !(e && e[0] == '0');
 }
 
-bool plan_cluster(const tl_attn *h, int nseq, int nmax, int ctas, Plan *p) {
+bool plan_cluster(const tl_attn *h, int nseq, int nmax, long long tot, int ctas, bool exchange, Plan *p) {
     const int G = h->nHead / h->nHeadKv;
-    if (!cluster_mode_allowed() || !decode_mma_covers(h->headDim, G, h->kvDtype)) return false;
-    constexpr int kTarget = 256, kMaxChunk = 512, kMaxCl = 8, kTile = 64;
+    if (!cluster_mode_allowed() || !decode_mma_covers(h->headDim, G, h->kvDtype) || nmax < 1) return false;
+    constexpr int kTarget = 256, kShortChunk = 512, kMaxCl = 8, kTile = 64;
     const int cl = std::max(1, std::min(kMaxCl, (nmax + kTarget - 1) / kTarget));
-    int chunk = (nmax + cl - 1) / cl;
-    chunk = std::max(kTile, (chunk + kTile - 1) / kTile * kTile);
-    if (chunk > kMaxChunk) return false;
+    long long chunk = (nmax + cl - 1) / cl;
+    chunk = std::max<long long>(kTile, (chunk + kTile - 1) / kTile * kTile);
     const long long grid = (long long)nseq * h->nHeadKv * cl;
-    if (grid > ctas) return false;
-    p->chunk = chunk;
+    if (grid > ctas || chunk > INT32_MAX / 2) return false;
+    const bool short_seqs = chunk <= kShortChunk;
+    const bool uniform = tot * 4 >= (long long)nseq * nmax * 3;
+    const bool fills = grid * 4 >= (long long)ctas * 3;
+    if (!short_seqs && !(uniform && fills)) return false;
+    if (exchange && grid / cl > decode_mma_cluster_capacity(h->headDim, G, h->kvDtype, cl)) return false;
+    p->chunk = (int)chunk;
     p->ctas = (int)grid;
     p->partial_floats = 0;
     p->cluster = cl;
@@ -172,7 +182,7 @@ bool plan_cluster(const tl_attn *h, int nseq, int nmax, int ctas, Plan *p) {
 }
 
 Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset, int slice,
-                 bool cluster_ok = false) {
+                 bool cluster_ok = false, bool exchange = false) {
     const int G = h->nHead / h->nHeadKv;
     const int occ = decode_ctas_per_sm(h->headDim, G, h->kvDtype);
     const int ctas = h->numSms * occ;
@@ -190,7 +200,7 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
         nmax = std::max(nmax, n);
     }
     Plan p{};
-    if (cluster_ok && plan_cluster(h, nseq, nmax, ctas, &p)) return p;
+    if (cluster_ok && plan_cluster(h, nseq, nmax, tot, ctas, exchange, &p)) return p;
     long long want = (tot * h->nHeadKv + (long long)ctas * 4 - 1) / ((long long)ctas * 4);
     int chunk = (int)std::min<long long>(1024, std::max<long long>(32, want));
     chunk = (chunk + 31) / 32 * 32;
@@ -213,8 +223,7 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
 int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, const int *pos_host,
                const float *q, float *out, cudaStream_t s, int pos_offset, float *lse_out,
                const DecodeArgs::Peer *px = nullptr) {
-    // cluster mode writes the output directly: not for partial (lse) or cross-GPU results
-    Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen, !px && !lse_out);
+    Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen, true, px != nullptr);
     TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
     DecodeArgs a{};
     a.q = q;
