@@ -131,6 +131,13 @@ TL_API int tl_decode_layer_host(tl_attn *h, int layer, int slot, const float *q,
  * headDim 64 the attention runs on the tcgen05 tensor-core kernel. */
 TL_API int tl_prefill_layer_host(tl_attn *h, int layer, int slot, const float *q, const float *k,
                           const float *v, int seqLen, float *ctx);
+/* Prefill that continues a cached prefix: the tokens sit at positions startPos..startPos+seqLen-1
+ * and token t attends cache positions 0..startPos+t.  It gives what the reference computes when
+ * it feeds a later prompt token by token through forwardDecode (src/tinylama.nim:70-73, each
+ * step src/forward.nim:314-317 with pos = curLen), in one call.  startPos = 0 is
+ * tl_prefill_layer_host.  TL_ERR_RANGE when startPos + seqLen > maxLen. */
+TL_API int tl_prefill_layer_at_host(tl_attn *h, int layer, int slot, int startPos, const float *q,
+                             const float *k, const float *v, int seqLen, float *ctx);
 /* Batched decode step with host buffers (the host-tier form of tl_decode_step): q
  * [nseq][nHead*headDim], k, v [nseq][nHeadKv*headDim], pos [nseq], out like q, all host
  * memory (pinned memory makes the copies asynchronous).  Synchronous.  A large batch (>= 0.3
@@ -160,6 +167,13 @@ TL_API int tl_decode_attention(tl_attn *h, int layer, int slot0, int nseq, const
  * otherwise fp32 CUDA cores, q and k are rotated in place. */
 TL_API int tl_prefill_step(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q, float *k,
                     const float *v, float *out, void *stream);
+/* tl_prefill_step continuing cached prefixes: token t of sequence b sits at position
+ * pos0_dev[b] + t and attends cache positions 0..pos0_dev[b]+t (the batched form of
+ * tl_prefill_layer_at_host).  pos0_host (optional, the same values on the host) is checked
+ * against maxLen before anything is launched. */
+TL_API int tl_prefill_step_at(tl_attn *h, int layer, int slot0, int nseq, int seqLen, const int *pos0_dev,
+                       const int *pos0_host, float *q, float *k, const float *v, float *out,
+                       void *stream);
 /* Same as tl_prefill_step but forces the fp32 CUDA-core attention kernel. */
 TL_API int tl_prefill_step_f32(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q,
                         float *k, const float *v, float *out, void *stream);

@@ -192,6 +192,70 @@ def test_prefill_step_batched(env, kvd, S):
         _lib.lib.tl_attn_destroy(h)
 
 
+@pytest.mark.parametrize("kvd", [0, 1])
+def test_prefill_step_at_continues_prefixes(env, kvd):
+    """tl_prefill_step_at: three sequences continue cached prefixes of 0, 300 and 1000 tokens
+    with 150 new tokens each (the prefill shape: 32 q / 8 kv heads, head_dim 64).  Each token is
+    checked against the reference's per-token path: RoPE at its position, store, attend every
+    position up to it (src/forward.nim:314-317)."""
+    torch, _lib = env
+    rng = np.random.default_rng(500 + kvd)
+    prefix = [0, 300, 1000]
+    B, Hq, Hkv, D, S, base = 3, 32, 8, 64, 150, 10000.0
+    maxLen = max(prefix) + S
+    h = create(_lib, 1, Hq, Hkv, D, maxLen, B, kvd, base)
+    try:
+        caches = []
+        for b, P in enumerate(prefix):
+            kc = np.zeros((Hkv * D, maxLen), np.float32)
+            vc = np.zeros((Hkv * D, maxLen), np.float32)
+            if P > 0:
+                k = randn(rng, Hkv * D, P)
+                v = randn(rng, Hkv * D, P)
+                kr = ora.rope_single(k, Hkv, D, D, base)
+                _lib.check(_lib.lib.tl_kv_store_host(h, 0, b, 0, kr.ctypes.data_as(C.c_void_p),
+                                                     v.ctypes.data_as(C.c_void_p), P))
+                kc[:, :P] = kr if kvd == 0 else bf16_round(kr)
+                vc[:, :P] = v if kvd == 0 else bf16_round(v)
+            caches.append((kc, vc))
+        q, k, v = randn(rng, B, S, Hq * D), randn(rng, B, S, Hkv * D), randn(rng, B, S, Hkv * D)
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        pos0 = np.array(prefix, np.int32)
+        dpos0 = torch.from_numpy(pos0).cuda()
+        out = torch.empty(B, S, Hq * D, device="cuda")
+        _lib.check(_lib.lib.tl_prefill_step_at(h, 0, 0, B, S, ptr(dpos0), pos0.ctypes.data_as(C.c_void_p),
+                                               ptr(dq), ptr(dk), ptr(dv), ptr(out), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+        got = out.cpu().numpy()
+        for b, P in enumerate(prefix):
+            kc, vc = caches[b]
+            out_ref, out_b = [], []
+            for t in range(S):
+                pos = P + t
+                qr = ora.rope_at_pos(q[b, t].reshape(-1, 1), Hq, D, D, base, pos)
+                kr = ora.rope_at_pos(k[b, t].reshape(-1, 1), Hkv, D, D, base, pos)
+                kc[:, pos:pos + 1] = kr if kvd == 0 else bf16_round(kr)
+                vc[:, pos:pos + 1] = v[b, t].reshape(-1, 1) if kvd == 0 else bf16_round(v[b, t].reshape(-1, 1))
+                out_ref.append(ora.attention_cached(qr, kc, vc, pos + 1, Hq, Hkv, D))
+                if kvd == 1:
+                    out_b.append(ora.attention_cached(bf16_round(qr), kc, vc, pos + 1, Hq, Hkv, D))
+            ref = np.concatenate(out_ref, axis=1)
+            g = np.ascontiguousarray(got[b].T)
+            if kvd == 0:
+                assert max_rel_err(g, ref) <= TOL_F32, (b, max_rel_err(g, ref))
+            else:
+                assert normwise_err(g, ref) <= TOL_BF16, (b, normwise_err(g, ref))
+                ref_b = np.concatenate(out_b, axis=1)
+                assert normwise_err(g, ref_b) <= 5e-3, (b, normwise_err(g, ref_b))
+        # a start past maxLen - S is refused before any launch
+        bad = np.array([0, 300, maxLen - S + 1], np.int32)
+        rc = _lib.lib.tl_prefill_step_at(h, 0, 0, B, S, ptr(dpos0), bad.ctypes.data_as(C.c_void_p),
+                                         ptr(dq), ptr(dk), ptr(dv), ptr(out), None)
+        assert rc != 0 and b"exceeds the KV cache" in _lib.lib.tl_last_error()
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
 @pytest.mark.parametrize("cluster", ["1", "0"])
 @pytest.mark.parametrize("exchange", ["peer", "nccl"])
 def test_dist_single_rank_matches_local(env, exchange, cluster):

@@ -221,6 +221,51 @@ def test_prefill_layer_matches_oracle_step(fa, S, kvd):
         assert normwise_err(ctx, ref_b) <= 5e-3, normwise_err(ctx, ref_b)
 
 
+def _decode_steps_ref(q, k, v, kc, vc, start, Hq, Hkv, D, base, kvd):
+    """The reference's way through a later prompt: one forwardDecode attention block per token
+    (src/forward.nim:314-317 at pos = start + t).  kc, vc are written in place; returns the ctx
+    columns, and for a bf16 cache also the ctx with q rounded to bf16 as the tensor cores see it."""
+    out, out_b = [], []
+    for t in range(q.shape[1]):
+        pos = start + t
+        qr = ora.rope_at_pos(q[:, t:t + 1], Hq, D, D, base, pos)
+        kr = ora.rope_at_pos(k[:, t:t + 1], Hkv, D, D, base, pos)
+        kc[:, pos:pos + 1] = kr if kvd == 0 else bf16_round(kr)
+        vc[:, pos:pos + 1] = v[:, t:t + 1] if kvd == 0 else bf16_round(v[:, t:t + 1])
+        out.append(ora.attention_cached(qr, kc, vc, pos + 1, Hq, Hkv, D))
+        if kvd == 1:
+            out_b.append(ora.attention_cached(bf16_round(qr), kc, vc, pos + 1, Hq, Hkv, D))
+    return np.concatenate(out, axis=1), (np.concatenate(out_b, axis=1) if out_b else None)
+
+
+@pytest.mark.parametrize("kvd", [0, 1])
+def test_prefill_layer_at_matches_decode_steps(fa, kvd):
+    """A prompt fed in chunks through prefillLayerAt (the first at position 0, each next one at
+    startPos = curLen) against the reference's multi-turn path, which feeds every token through
+    forwardDecode (src/tinylama.nim:70-73).  Chunk boundaries fall inside the 128-key tiles; a
+    bf16 cache with head_dim 64 runs the tcgen05 kernel with its key range shifted by startPos."""
+    rng = np.random.default_rng(77 + kvd)
+    chunks = [130, 77, 200, 1]
+    total = sum(chunks)
+    cache = fa.initKvCache(hp(fa), total + 5, kv_dtype=kvd)
+    kc = np.zeros((256, total + 5), np.float32)
+    vc = np.zeros((256, total + 5), np.float32)
+    start = 0
+    for S in chunks:
+        q, k, v = randn(rng, 2048, S), randn(rng, 256, S), randn(rng, 256, S)
+        ctx = fa.prefillLayerAt(cache, 0, start, q, k, v)
+        ref, ref_b = _decode_steps_ref(q, k, v, kc, vc, start, 32, 4, 64, 10000.0, kvd)
+        if kvd == 0:
+            assert max_rel_err(ctx, ref) <= TOL_F32, (start, max_rel_err(ctx, ref))
+        else:
+            assert normwise_err(ctx, ref) <= TOL_BF16, (start, normwise_err(ctx, ref))
+            assert normwise_err(ctx, ref_b) <= 5e-3, (start, normwise_err(ctx, ref_b))
+        start += S
+    z = np.zeros((2048, 6), np.float32)
+    with pytest.raises(ValueError, match="exceeds the KV cache"):
+        fa.prefillLayerAt(cache, 0, start, z, z[:256], z[:256])
+
+
 def test_prefill_overflow_is_refused(fa):
     cache = fa.initKvCache(hp(fa), 8)
     z = np.zeros((2048, 9), np.float32)

@@ -49,11 +49,13 @@ SIGNATURES = {
     "tl_attention_cached_host": (_I, [_P, _I, _I, _P, _I, _I, _I, _I, _P]),
     "tl_decode_layer_host": (_I, [_P, _I, _I, _P, _P, _P, _I, _P]),
     "tl_prefill_layer_host": (_I, [_P, _I, _I, _P, _P, _P, _I, _P]),
+    "tl_prefill_layer_at_host": (_I, [_P, _I, _I, _I, _P, _P, _P, _I, _P]),
     "tl_decode_batch_host": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "tl_decode_step": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "tl_decode_attention": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "tl_prefill_step": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "tl_prefill_step_f32": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "tl_prefill_step_at": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "tl_kv_store": (_I, [_P, _I, _I, _I, _P, _P, _I, _P]),
     "tl_check_device": (_I, [_P, _P]),
     "tl_decode_attention_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),

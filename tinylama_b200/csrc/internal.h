@@ -220,7 +220,7 @@ struct PrefillArgs {
     unsigned *err;
 };
 cudaError_t launch_prefill_f32(const PrefillArgs &a, cudaStream_t s);
-// tcgen05 / TMEM bf16 path (bf16 cache, headDim 64, pos0 == 0).  Returns
+// tcgen05 / TMEM bf16 path (bf16 cache, headDim 64; pos0 as above).  Returns
 // cudaErrorNotSupported when the shape is not covered.
 cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s);
 

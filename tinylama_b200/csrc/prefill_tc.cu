@@ -2,6 +2,9 @@
 //
 // Replaces the context part of attentionFull (src/forward.nim:141-176) on the bf16 KV path:
 // for q-head h and query i, s_j = q_i . k_j / sqrt(d) for j <= i, softmax, ctx_i = sum p_j v_j.
+// A prefill may also continue a cached prefix (the prompt of a later turn, which the reference
+// feeds token by token through forwardDecode, src/tinylama.nim:70-73): query i of a sequence
+// whose chunk starts at position pos0 attends cache positions j <= pos0 + i.
 // Inputs are bf16 (Q staged by the RoPE kernel, K/V from the cache the same launch sequence
 // appended to), products accumulate in fp32 in tensor memory, softmax runs in fp32.
 //
@@ -196,6 +199,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 struct TcParams {
     HeadView out;
+    const int *pos0;       // device [nseq]: token t of sequence b sits at position pos0[b] + t, or
+                           // nullptr (all zero).  Its keys are cache positions [0, pos0[b] + t].
     int nseq, ntok, nHead, nHeadKv;
     int64_t kv_row_layer;  // cache row of (layer, slot0, kvh=0, pos=0)
     int kv_rows_per_slot;  // nHeadKv * maxLen
@@ -313,10 +318,11 @@ struct Bars {
 
 // One work tile: NQ*128 query rows of one (sequence, q-head).  Tiles are numbered heaviest first
 // (the last query rows of a sequence attend to the most keys); CTA i takes tiles i, i + gridDim,
-// ... so every CTA gets a similar mix.
+// ... so every CTA gets a similar mix.  off = the position of the sequence's first query (a
+// prefill that continues a cached prefix); query row r attends keys [0, off + r].
 template <int NQ, int BN_>
 struct TileInfo {
-    int b, h, g, q0, nkv, nq_live, qrow, kvrow0;
+    int b, h, g, q0, off, nkv, nq_live, qrow, kvrow0;
     int nt[NQ];
     __device__ __forceinline__ TileInfo(const TcParams &p, int t) {
         const int ngroups = (p.ntok + NQ * BM - 1) / (NQ * BM);
@@ -326,12 +332,15 @@ struct TileInfo {
         b = rem - h * p.nseq;
         g = h / (p.nHead / p.nHeadKv);
         q0 = (ngroups - 1 - rank) * NQ * BM;
+        // the host checks 0 <= pos0 and pos0 + ntok <= maxLen; the clamp keeps every K/V tile
+        // inside this (sequence, kv-head)'s rows whatever the device array holds
+        off = p.pos0 ? min(max(p.pos0[b], 0), p.maxLen - p.ntok) : 0;
         nkv = 0;
         nq_live = 0;
 #pragma unroll
         for (int q = 0; q < NQ; ++q) {
             const int start = q0 + q * BM;
-            nt[q] = start < p.ntok ? (min(start + BM, p.ntok) + BN_ - 1) / BN_ : 0;
+            nt[q] = start < p.ntok ? (off + min(start + BM, p.ntok) + BN_ - 1) / BN_ : 0;
             nkv = max(nkv, nt[q]);
             nq_live += nt[q] > 0;
         }
@@ -533,6 +542,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             if (ntq == 0) continue;
             const int row_first = ti.q0 + q * BM;
             const int row = row_first + r;
+            const int kpos_first = ti.off + row_first, kpos = ti.off + row;  // last key of a row
             float m_run = -INFINITY, l = 0.f;
             for (int j = 0; j < ntq && ok; ++j) {
                 // warp-uniform verdict: the TMEM loads below are warp-collective
@@ -550,10 +560,11 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
                 tc_fence_before();
                 mbar_arrive(&bars->s_free[q]);  // S_q(j) is in registers: the next S may overwrite it
                 const int k0 = j * BNK;
-                if (k0 + BNK - 1 > row_first || k0 + BNK > p.ntok) {  // tile crosses the diagonal or the end
+                const int kend = ti.off + p.ntok;
+                if (k0 + BNK - 1 > kpos_first || k0 + BNK > kend) {  // tile crosses the diagonal or the end
 #pragma unroll
                     for (int c = 0; c < BNK; ++c)
-                        if (k0 + c > row || k0 + c >= p.ntok) sr[c] = __float_as_uint(-INFINITY);
+                        if (k0 + c > kpos || k0 + c >= kend) sr[c] = __float_as_uint(-INFINITY);
                 }
                 // row maximum: four independent chains of three-input max
                 float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -699,6 +710,7 @@ cudaError_t launch_shape(const PrefillArgs &a, cudaStream_t s) {
         return cudaErrorNotSupported;
     TcParams p;
     p.out = a.out;
+    p.pos0 = a.pos0;
     p.nseq = a.nseq;
     p.ntok = a.ntok;
     p.nHead = a.nHead;
@@ -734,8 +746,8 @@ cudaError_t launch_shape(const PrefillArgs &a, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_prefill_tc(const PrefillArgs &a, cudaStream_t s) {
-    if (a.headDim != HD || a.kv.dtype != TL_KV_BF16 || a.qb == nullptr || a.pos0 != nullptr ||
-        a.kf.ptr != nullptr)
+    if (a.headDim != HD || a.kv.dtype != TL_KV_BF16 || a.qb == nullptr || a.kf.ptr != nullptr ||
+        a.ntok > a.kv.maxLen)
         return cudaErrorNotSupported;
     return launch_shape<2, 128>(a, s);
 }

@@ -300,14 +300,17 @@ HeadView tok_view(float *p, int H, int D, int S) {
     return v;
 }
 
+// q_rotated: the fp32 q view holds the rotated q (the RoPE kernel wrote it back); without it
+// only the tensor-core path, which reads the bf16 copy, can run.
 int prefill_attention(tl_attn *h, int layer, int slot0, int nseq, int S, HeadView q, HeadView out,
-                      bool qb_ready, bool force_f32, cudaStream_t s) {
+                      bool qb_ready, bool force_f32, cudaStream_t s, const int *pos0_dev = nullptr,
+                      bool q_rotated = true) {
     PrefillArgs a{};
     a.q = q;
     a.out = out;
     a.kf.ptr = nullptr;
     a.vf.ptr = nullptr;
-    a.pos0 = nullptr;
+    a.pos0 = pos0_dev;
     a.nseq = nseq;
     a.ntok = S;
     a.nHead = h->nHead;
@@ -322,6 +325,8 @@ int prefill_attention(tl_attn *h, int layer, int slot0, int nseq, int S, HeadVie
         cudaError_t e = launch_prefill_tc(a, s);
         if (e == cudaSuccess) return TL_OK;
         if (e != cudaErrorNotSupported) TL_CUDA(e);
+        if (!q_rotated)
+            return fail(TL_ERR_UNSUPPORTED, "prefill: the tensor-core kernel could not be set up for this shape");
     }
     cudaError_t e = launch_prefill_f32(a, s);
     if (e == cudaErrorNotSupported) return fail(TL_ERR_UNSUPPORTED, "prefill: shape not covered");
@@ -764,13 +769,15 @@ int tl_decode_batch_host(tl_attn *h, int layer, int slot0, int nseq, const int *
     return finish(h, h->stream);
 }
 
-int tl_prefill_layer_host(tl_attn *h, int layer, int slot, const float *q, const float *k,
-                          const float *v, int seqLen, float *ctx) {
+static int prefill_layer_host_impl(tl_attn *h, int layer, int slot, int startPos, const float *q,
+                                   const float *k, const float *v, int seqLen, float *ctx) {
     if (!h || !q || !k || !v || !ctx) return fail(TL_ERR_INVALID, "NULL argument");
     TL_TRY(check_layer_slot(h, layer, slot));
     if (seqLen < 0) return fail(TL_ERR_INVALID, "seqLen < 0");
-    if (seqLen > h->maxLen)
-        return fail(TL_ERR_RANGE, "prefill of %d tokens exceeds the KV cache (maxLen %d)", seqLen, h->maxLen);
+    if (startPos < 0) return fail(TL_ERR_INVALID, "negative start position");
+    if ((long long)startPos + seqLen > h->maxLen)
+        return fail(TL_ERR_RANGE, "prefill of positions [%d, %d) exceeds the KV cache (maxLen %d)", startPos,
+                    startPos + seqLen, h->maxLen);
     if (seqLen == 0) return TL_OK;
     DeviceGuard g(h->device);
     const int D = h->headDim, Hq = h->nHead, Hk = h->nHeadKv;
@@ -780,6 +787,12 @@ int tl_prefill_layer_host(tl_attn *h, int layer, int slot, const float *q, const
     TL_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
     TL_CUDA(cudaMemcpyAsync(dk, k, nk * 4, cudaMemcpyHostToDevice, h->stream));
     TL_CUDA(cudaMemcpyAsync(dv, v, nk * 4, cudaMemcpyHostToDevice, h->stream));
+    const int *pos0_dev = nullptr;
+    if (startPos > 0) {
+        // the attention kernels take the start position from device memory
+        TL_CUDA(cudaMemcpyAsync(h->dPos, &startPos, sizeof(int), cudaMemcpyHostToDevice, h->stream));
+        pos0_dev = h->dPos;
+    }
     const bool tc = tc_prefill_eligible(h);
     if (tc) TL_TRY(ensure_qb(h, nq * 2));
     RopeAppendArgs a = rope_args(h);
@@ -791,16 +804,26 @@ int tl_prefill_layer_host(tl_attn *h, int layer, int slot, const float *q, const
     a.nHead = Hq;
     a.nHeadKv = Hk;
     a.headDim = D;
-    a.pos0_scalar = 0;
+    a.pos0_scalar = startPos;
     a.rope_q = a.rope_k = a.store = true;
     a.layer = layer;
     a.slot0 = slot;
     a.qb = tc ? h->dQb : nullptr;
     TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), h->stream));
     TL_TRY(prefill_attention(h, layer, slot, 1, seqLen, col_view(dq, Hq, D, seqLen),
-                             col_view(dc, Hq, D, seqLen), tc, false, h->stream));
+                             col_view(dc, Hq, D, seqLen), tc, false, h->stream, pos0_dev));
     TL_CUDA(cudaMemcpyAsync(ctx, dc, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     return finish(h, h->stream);
+}
+
+int tl_prefill_layer_host(tl_attn *h, int layer, int slot, const float *q, const float *k,
+                          const float *v, int seqLen, float *ctx) {
+    return prefill_layer_host_impl(h, layer, slot, 0, q, k, v, seqLen, ctx);
+}
+
+int tl_prefill_layer_at_host(tl_attn *h, int layer, int slot, int startPos, const float *q, const float *k,
+                             const float *v, int seqLen, float *ctx) {
+    return prefill_layer_host_impl(h, layer, slot, startPos, q, k, v, seqLen, ctx);
 }
 
 // ---- device tier -------------------------------------------------------------------------------
@@ -845,12 +868,20 @@ int tl_decode_attention(tl_attn *h, int layer, int slot0, int nseq, const int *p
 }
 
 static int prefill_step_impl(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q,
-                             float *k, const float *v, float *out, void *stream, bool force_f32) {
+                             float *k, const float *v, float *out, void *stream, bool force_f32,
+                             const int *pos0_dev = nullptr, const int *pos0_host = nullptr) {
     if (!h || !q || !k || !v || !out) return fail(TL_ERR_INVALID, "NULL argument");
     TL_TRY(check_layer_slot(h, layer, slot0, nseq));
     if (seqLen < 0) return fail(TL_ERR_INVALID, "seqLen < 0");
     if (seqLen > h->maxLen)
         return fail(TL_ERR_RANGE, "prefill of %d tokens exceeds the KV cache (maxLen %d)", seqLen, h->maxLen);
+    if (pos0_host)
+        for (int b = 0; b < nseq; ++b) {
+            if (pos0_host[b] < 0) return fail(TL_ERR_INVALID, "negative start position");
+            if ((long long)pos0_host[b] + seqLen > h->maxLen)
+                return fail(TL_ERR_RANGE, "prefill of positions [%d, %d) exceeds the KV cache (maxLen %d)",
+                            pos0_host[b], pos0_host[b] + seqLen, h->maxLen);
+        }
     if (seqLen == 0) return TL_OK;
     DeviceGuard g(h->device);
     cudaStream_t s = pick(h, stream);
@@ -866,6 +897,7 @@ static int prefill_step_impl(tl_attn *h, int layer, int slot0, int nseq, int seq
     a.nHead = Hq;
     a.nHeadKv = Hk;
     a.headDim = D;
+    a.pos0 = pos0_dev;
     a.pos0_scalar = 0;
     a.rope_q = a.rope_k = a.store = true;
     // the tensor-core path reads the bf16 copy of q and the cache, so the rotated fp32 q and k
@@ -876,7 +908,13 @@ static int prefill_step_impl(tl_attn *h, int layer, int slot0, int nseq, int seq
     a.qb = tc ? h->dQb : nullptr;
     TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), s));
     return prefill_attention(h, layer, slot0, nseq, seqLen, tok_view(q, Hq, D, seqLen),
-                             tok_view(out, Hq, D, seqLen), tc, force_f32, s);
+                             tok_view(out, Hq, D, seqLen), tc, force_f32, s, pos0_dev, !tc);
+}
+
+int tl_prefill_step_at(tl_attn *h, int layer, int slot0, int nseq, int seqLen, const int *pos0_dev,
+                       const int *pos0_host, float *q, float *k, const float *v, float *out, void *stream) {
+    if (!pos0_dev) return fail(TL_ERR_INVALID, "NULL argument");
+    return prefill_step_impl(h, layer, slot0, nseq, seqLen, q, k, v, out, stream, false, pos0_dev, pos0_host);
 }
 
 int tl_prefill_step(tl_attn *h, int layer, int slot0, int nseq, int seqLen, float *q, float *k,

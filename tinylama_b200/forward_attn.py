@@ -240,6 +240,21 @@ def prefillLayer(cache: KvCache, layer: int, q: np.ndarray, k: np.ndarray, v: np
     return ctx
 
 
+def prefillLayerAt(cache: KvCache, layer: int, startPos: int, q: np.ndarray, k: np.ndarray,
+                   v: np.ndarray, slot: int = 0) -> np.ndarray:
+    """The attention blocks of S successive forwardDecode steps from pos = startPos
+    (src/forward.nim:314-317 for pos = startPos .. startPos+S-1: the reference's multi-turn
+    path feeds a later prompt this way, src/tinylama.nim:70-73) in one call: q, k, v are
+    [.., S] columns, token t is rotated at startPos + t, stored there, and attends positions
+    0..startPos+t.  The caller advances curLen to startPos + S."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    S = q.shape[1]
+    ctx = np.empty((cache.hp.nHead * cache.headDim, S), np.float32)
+    check(lib.tl_prefill_layer_at_host(cache.handle, layer, slot, int(startPos), _fp(q), _fp(k), _fp(v),
+                                       S, _fp(ctx)))
+    return ctx
+
+
 def forwardDecodeCheck(cache: KvCache) -> None:
     """The guard at the top of forwardDecode (src/forward.nim:290-291)."""
     if cache.curLen >= cache.maxLen:
