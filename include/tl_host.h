@@ -47,6 +47,12 @@ typedef struct tlh_attn_ops {
                             int nHeadKv, int headDim, float *out);
     /* KvCache.curLen / maxLen */
     int curLen, maxLen;
+    /* Optional (NULL when the table does not provide it).  The attention blocks of seqLen
+     * successive forwardDecode steps from pos = startPos (src/forward.nim:314-317), in one
+     * call: RoPE q, k at startPos + t, storeKVRange at startPos, token t attending positions
+     * 0..startPos+t; out = [nHead*headDim, seqLen]. */
+    int (*prefill_at)(void *ctx, int layer, int startPos, const float *q, const float *k, const float *v,
+                      int seqLen, float *out);
 } tlh_attn_ops;
 
 typedef struct tlh_model tlh_model;
@@ -79,7 +85,20 @@ TLH_API int tlh_model_tensor(const tlh_model *m, const char *name, float *out, l
 TLH_API long tlh_generate(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int nPrompt,
                           int nNew, int32_t *outIds, float *gaps, float *attnOut, long attnCap);
 
-/* The attention procs on the B200 (libtlattn.so, one cache slot, f32 cache). */
+/* The REPL of src/tinylama.nim:45-100, one line at a time.  tlh_session_init is the
+ * initKvCache(max(32, nNew + 32)) of :47 (the cache then lives across turns).  tlh_run_prompt
+ * is runPrompt (:49-86) for one line's tokens: the first turn (curLen = 0) runs forwardPrefill;
+ * a later turn feeds its tokens through forwardDecode one at a time (:70-73) -- or, with
+ * chunked != 0 and a table that has prefill_at, through one forward pass over all of them at
+ * positions curLen.. (the same attention, fewer passes over the weights) -- and both then
+ * decode nNew - 1 greedy tokens.  Outputs as tlh_generate; the attention outputs of a chunked
+ * later turn are [nLayer][nHead*headDim*nPrompt].  Returns the number of attention floats. */
+TLH_API int tlh_session_init(tlh_attn_ops *ops, int nNew);
+TLH_API long tlh_run_prompt(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int nPrompt, int nNew,
+                            int chunked, int32_t *outIds, float *gaps, float *attnOut, long attnCap);
+
+/* The attention procs on the B200 (libtlattn.so, one cache slot, f32 cache); the table has
+ * prefill_at (tl_prefill_layer_at_host). */
 TLH_API tlh_attn_ops *tlh_gpu_attn_ops_create(int nLayer, int nHead, int nHeadKv, int headDim,
                                               int ropeDim, float ropeBase, int device);
 TLH_API void tlh_gpu_attn_ops_destroy(tlh_attn_ops *ops);

@@ -18,7 +18,8 @@ LIB = os.path.join(HERE, "liboracle.so")
 
 
 def build() -> str:
-    srcs = [os.path.join(HERE, f) for f in ("attn_oracle.c", "attn_ops_oracle.c", "attn_oracle.h")]
+    srcs = [os.path.join(HERE, f) for f in ("attn_oracle.c", "attn_ops_oracle.c", "attn_oracle.h",
+                                            os.path.join("..", "include", "tl_host.h"))]
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
     return LIB

@@ -70,3 +70,29 @@ class NumpyModel:
             logits = self.forward([ids[-1]], kc, vc, pos, dump)
             pos += 1
         return np.array(ids), np.array(gaps), dump
+
+    def repl(self, lines, n_new, max_len):
+        """The REPL of src/tinylama.nim:45-100 over several lines on one cache: the first line is
+        prefilled; a later line's tokens go in at positions curLen.. (one forwardDecode each in
+        the reference; the same attention in one numpy pass here).  Each line then decodes
+        n_new - 1 greedy tokens; the last greedy id of a line is never fed back."""
+        hp = self.hp
+        kvDim = hp["nHeadKv"] * (hp["nEmb"] // hp["nHead"])
+        kc = [np.zeros((kvDim, max_len), np.float32) for _ in range(hp["nLayer"])]
+        vc = [np.zeros((kvDim, max_len), np.float32) for _ in range(hp["nLayer"])]
+        out, pos = [], 0
+        for line in lines:
+            dump, ids, gaps = [], [], []
+            logits = self.forward(list(line), kc, vc, pos, dump)
+            pos += len(line)
+            for j in range(n_new):
+                col = logits[:, -1]
+                order = np.argsort(col)
+                ids.append(int(order[-1]))
+                gaps.append(float(col[order[-1]] - col[order[-2]]))
+                if j == n_new - 1:
+                    break
+                logits = self.forward([ids[-1]], kc, vc, pos, dump)
+                pos += 1
+            out.append((np.array(ids), np.array(gaps), dump))
+        return out

@@ -83,6 +83,56 @@ def test_forward_with_oracle_attention_matches_numpy(small_model):
         m.close()
 
 
+def _per_token_layout(dump, n_layer, width, n_tokens):
+    """Attention outputs of a line fed in one pass ([nLayer][width, S] columns) in the order
+    the per-token path writes them ([token][nLayer][width])."""
+    a = dump.reshape(n_layer, width, n_tokens)
+    return np.ascontiguousarray(a.transpose(2, 0, 1)).reshape(-1)
+
+
+def test_repl_lines_match_numpy(small_model):
+    """Three REPL lines on one cache with the oracle's attention procs: the first prefilled,
+    the later ones fed token by token through forwardDecode (src/tinylama.nim:70-73), against
+    the numpy forward; then the same lines through the oracle table, which has no prefill_at,
+    asking for chunked input (it keeps the per-token path)."""
+    from tinylama_b200.host_api import Model
+    path, keep = small_model
+    m = Model(path, nthreads=2)
+    rng = np.random.default_rng(3)
+    lines = [rng.integers(3, 512, size=n).astype(np.int32) for n in (8, 5, 6)]
+    n_new = 4
+    npm = _numpy_model(keep, dict(nLayer=2, nEmb=256, nHead=4, nHeadKv=2, base=10000.0, eps=1e-5))
+    ref = npm.repl(lines, n_new, max(32, n_new + 32))
+    ops = ora.lib().ora_attn_ops_create(m.hp.nLayer, m.hp.nHeadKv, m.hp.nEmb // m.hp.nHead)
+    try:
+        for chunked in (False, True):
+            m.session_init(ops, n_new)
+            for li, line in enumerate(lines):
+                ids, gaps, dump = m.run_prompt(ops, line, n_new, chunked=chunked)
+                nids, ngaps, ndump = ref[li]
+                flat = lambda ds: np.concatenate([d.reshape(-1) for d in ds])
+                if li == 0:
+                    r = flat(ndump)
+                else:
+                    # numpy fed the line in one pass; the per-token path writes token by token
+                    r = np.concatenate([_per_token_layout(flat(ndump[:2]), 2, 256, len(line)), flat(ndump[2:])])
+                assert r.size == dump.size, (li, r.size, dump.size)
+                assert np.max(np.abs(dump - r)) <= 1e-3 * np.max(np.abs(r)), li
+                for j in range(n_new):
+                    if ngaps[j] > 1e-3:
+                        assert ids[j] == nids[j], (li, j, ids, nids)
+                    else:
+                        break
+        # the cache is shared across lines: it fills up like the reference's
+        m.session_init(ops, 1)  # maxLen 33
+        m.run_prompt(ops, rng.integers(3, 512, size=30).astype(np.int32), 1)
+        with pytest.raises(ValueError, match="KV cache full"):
+            m.run_prompt(ops, rng.integers(3, 512, size=4).astype(np.int32), 1)
+    finally:
+        ora.lib().ora_attn_ops_destroy(ops)
+        m.close()
+
+
 def test_forward_errors_follow_the_reference(small_model):
     from tinylama_b200 import host_api
     with pytest.raises(ValueError, match="cannot open"):

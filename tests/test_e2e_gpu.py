@@ -67,3 +67,49 @@ def test_tinyllama_greedy_ids_identical(tinyllama):
           f"normwise {worst_norm:.2e}, floored elementwise {worst_floor:.2e}")
     assert worst_norm <= 1e-3, worst_norm
     assert np.array_equal(ids_g, ids_o), (ids_g, ids_o, gaps_o)
+
+
+def test_tinyllama_repl_lines_chunked(tinyllama):
+    """The REPL (src/tinylama.nim:45-100): three lines on one cache.  The reference feeds a later
+    line token by token through forwardDecode (:70-73); the B200 table also takes it in one
+    pass at positions curLen.. (prefill_at = tl_prefill_layer_at_host).  Ids of all three runs
+    (oracle per token, B200 per token, B200 chunked) must be identical, and the chunked run's
+    attention outputs, reordered per token, agree with the oracle's."""
+    from tinylama_b200 import host_api
+    m = tinyllama
+    hp = m.hp
+    width = hp.nHead * (hp.nEmb // hp.nHead)
+    rng = np.random.default_rng(SEED + 1)
+    lines = [rng.integers(3, 32000, size=n).astype(np.int32) for n in (8, 5, 6)]
+    n_new = 4
+    ops_o = ora.lib().ora_attn_ops_create(hp.nLayer, hp.nHeadKv, hp.nEmb // hp.nHead)
+    ops_g = host_api.gpu_attn_ops(hp)
+    runs = {}
+    try:
+        for name, ops, chunked in (("oracle", ops_o, False), ("b200", ops_g, False), ("b200_chunked", ops_g, True)):
+            m.session_init(ops, n_new)
+            runs[name] = [m.run_prompt(ops, line, n_new, chunked=chunked) for line in lines]
+    finally:
+        ora.lib().ora_attn_ops_destroy(ops_o)
+        host_api.free_gpu_attn_ops(ops_g)
+    worst = 0.0
+    for li, line in enumerate(lines):
+        ids_o, gaps_o, dump_o = runs["oracle"][li]
+        for name in ("b200", "b200_chunked"):
+            assert np.array_equal(runs[name][li][0], ids_o), (name, li, runs[name][li][0], ids_o, gaps_o)
+        dump_c = runs["b200_chunked"][li][2]
+        if li > 0:
+            S = len(line)
+            head = dump_c[:hp.nLayer * width * S].reshape(hp.nLayer, width, S).transpose(2, 0, 1).reshape(-1)
+            dump_c = np.concatenate([head, dump_c[hp.nLayer * width * S:]])
+        assert dump_c.size == dump_o.size
+        # per layer: the first line's prefill outputs [width, S], then one column per token
+        sizes = ([width * len(line)] * hp.nLayer if li == 0 else []) + \
+            [width] * ((dump_o.size - (hp.nLayer * width * len(line) if li == 0 else 0)) // width)
+        off = 0
+        for size in sizes:
+            worst = max(worst, normwise_err(dump_c[off:off + size], dump_o[off:off + size]))
+            off += size
+        assert off == dump_o.size
+    print(f"\nREPL ids {[r[0].tolist() for r in runs['oracle']]}; chunked attention normwise {worst:.2e}")
+    assert worst <= 1e-3, worst

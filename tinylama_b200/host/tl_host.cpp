@@ -375,14 +375,22 @@ struct Dump {
     }
 };
 
-// forwardPrefill (src/forward.nim:243-284) / forwardDecode (:286-329)
-int forward(tlh_model *m, tlh_attn_ops *ops, const std::vector<int32_t> &tokens, bool prefill, Tensor &logits,
+enum class Pass { Prefill, Decode, Continue };
+
+// forwardPrefill (src/forward.nim:243-284) / forwardDecode (:286-329).  Continue: the tokens sit
+// at positions curLen.. and attend the cache (ops->prefill_at): what feeding them one by one
+// through forwardDecode computes, in one pass; logits of every column, the last one used.
+int forward(tlh_model *m, tlh_attn_ops *ops, const std::vector<int32_t> &tokens, Pass mode, Tensor &logits,
             Dump &dump) {
+    const bool prefill = mode == Pass::Prefill;
     const tlh_hparams &hp = m->hp;
     if (!m->arch.empty() && m->arch != "llama") return fail(-1, "unsupported architecture: %s", m->arch.c_str());
     if (hp.nHeadKv != 0 && hp.nHead % hp.nHeadKv != 0)
         return fail(-1, "GQA requires head_count divisible by head_count_kv");
     if (!prefill && ops->curLen >= ops->maxLen) return fail(-3, "KV cache full");
+    if (mode == Pass::Continue && !ops->prefill_at) return fail(-1, "attention table has no prefill_at");
+    if (mode == Pass::Continue && (long)ops->curLen + (long)tokens.size() > ops->maxLen)
+        return fail(-3, "KV cache full");
     const int headDim = hp.nEmb / hp.nHead;
     const int ropeDim = hp.ropeDim > 0 ? hp.ropeDim : headDim;
     const int S = (int)tokens.size();
@@ -406,7 +414,11 @@ int forward(tlh_model *m, tlh_attn_ops *ops, const std::vector<int32_t> &tokens,
         Tensor k = linear(xn, *wk, m->nthreads);
         const Tensor v = linear(xn, *wv, m->nthreads);
         Tensor ctx(hp.nHead * headDim, S);
-        if (prefill) {
+        if (mode == Pass::Continue) {
+            if ((rc = ops->prefill_at(ops->ctx, layer, pos, q.data.data(), k.data.data(), v.data.data(), S,
+                                      ctx.data.data())))
+                return rc;
+        } else if (prefill) {
             if ((rc = ops->rope_single(ops->ctx, q.data.data(), hp.nHead, headDim, ropeDim, hp.ropeFreqBase, S)) ||
                 (rc = ops->rope_single(ops->ctx, k.data.data(), hp.nHeadKv, headDim, ropeDim, hp.ropeFreqBase, S)) ||
                 (rc = ops->store_kv(ops->ctx, layer, 0, k.data.data(), v.data.data(), (int)k.shape[0], S)) ||
@@ -426,7 +438,8 @@ int forward(tlh_model *m, tlh_attn_ops *ops, const std::vector<int32_t> &tokens,
         const Tensor xn2 = rmsnorm_cols(x, *fn, hp.rmsEps);
         add_inplace(x, ffn(xn2, *wg, *wu, *wd, m->nthreads));
     }
-    if (!prefill) ops->curLen = pos + 1;
+    if (mode == Pass::Decode) ops->curLen = pos + 1;
+    if (mode == Pass::Continue) ops->curLen = pos + S;
     const Tensor *nw = tensor_or(m, "norm.weight", "output_norm.weight");
     const Tensor *ow = tensor(m, "output.weight");
     if (!nw || !ow) return fail(-1, "missing output tensors");
@@ -487,6 +500,12 @@ int g_full(void *c, const float *q, const float *k, const float *v, int S, int n
 int g_cached(void *c, int layer, const float *q, int curLen, int nH, int nKv, int d, float *out) {
     GpuOps *g = (GpuOps *)c;
     const int rc = tl_attention_cached_host(g->h, layer, 0, q, curLen, nH, nKv, d, out);
+    return rc ? fail(rc, "%s", tl_last_error()) : 0;
+}
+
+int g_prefill_at(void *c, int layer, int start, const float *q, const float *k, const float *v, int S, float *out) {
+    GpuOps *g = (GpuOps *)c;
+    const int rc = tl_prefill_layer_at_host(g->h, layer, 0, start, q, k, v, S, out);
     return rc ? fail(rc, "%s", tl_last_error()) : 0;
 }
 
@@ -652,11 +671,43 @@ long tlh_generate(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int nP
     Dump dump{attnOut, attnCap};
     std::vector<int32_t> toks(prompt, prompt + nPrompt);
     Tensor logits;
-    if ((rc = forward(m, ops, toks, true, logits, dump))) return rc;
+    if ((rc = forward(m, ops, toks, Pass::Prefill, logits, dump))) return rc;
     int32_t next = argmax_last(logits, m->hp.nVocab, gaps ? &gaps[0] : nullptr);
     outIds[0] = next;
     for (int j = 1; j < nNew; ++j) {
-        if ((rc = forward(m, ops, std::vector<int32_t>{next}, false, logits, dump))) return rc;
+        if ((rc = forward(m, ops, std::vector<int32_t>{next}, Pass::Decode, logits, dump))) return rc;
+        next = argmax_last(logits, m->hp.nVocab, gaps ? &gaps[j] : nullptr);
+        outIds[j] = next;
+    }
+    return dump.n;
+}
+
+int tlh_session_init(tlh_attn_ops *ops, int nNew) {
+    if (!ops || nNew <= 0) return fail(-1, "bad argument");
+    return ops->init_cache(ops->ctx, std::max(32, nNew + 32));  // src/tinylama.nim:47
+}
+
+long tlh_run_prompt(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int nPrompt, int nNew, int chunked,
+                    int32_t *outIds, float *gaps, float *attnOut, long attnCap) {
+    if (!m || !ops || !prompt || nPrompt <= 0 || nNew <= 0 || !outIds) return fail(-1, "bad argument");
+    Dump dump{attnOut, attnCap};
+    std::vector<int32_t> toks(prompt, prompt + nPrompt);
+    Tensor logits;
+    int rc = 0;
+    if (ops->curLen == 0) {
+        // the first line: forwardPrefill over its tokens (src/tinylama.nim:53-55)
+        if ((rc = forward(m, ops, toks, Pass::Prefill, logits, dump))) return rc;
+    } else if (chunked && ops->prefill_at) {
+        if ((rc = forward(m, ops, toks, Pass::Continue, logits, dump))) return rc;
+    } else {
+        // a later line: one forwardDecode per token (src/tinylama.nim:70-73)
+        for (int32_t t : toks)
+            if ((rc = forward(m, ops, std::vector<int32_t>{t}, Pass::Decode, logits, dump))) return rc;
+    }
+    int32_t next = argmax_last(logits, m->hp.nVocab, gaps ? &gaps[0] : nullptr);
+    outIds[0] = next;
+    for (int j = 1; j < nNew; ++j) {
+        if ((rc = forward(m, ops, std::vector<int32_t>{next}, Pass::Decode, logits, dump))) return rc;
         next = argmax_last(logits, m->hp.nVocab, gaps ? &gaps[j] : nullptr);
         outIds[j] = next;
     }
@@ -680,6 +731,7 @@ tlh_attn_ops *tlh_gpu_attn_ops_create(int nLayer, int nHead, int nHeadKv, int he
     g->ops.store_kv = g_store;
     g->ops.attention_full = g_full;
     g->ops.attention_cached = g_cached;
+    g->ops.prefill_at = g_prefill_at;
     return &g->ops;  // ops is the first member: the pointer is also the GpuOps*
 }
 

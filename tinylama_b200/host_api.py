@@ -31,6 +31,10 @@ lib.tlh_model_tensor.argtypes = [_P, C.c_char_p, _P, _L, C.POINTER(_L)]
 lib.tlh_model_tensor.restype = _I
 lib.tlh_generate.argtypes = [_P, _P, _P, _I, _I, _P, _P, _P, _L]
 lib.tlh_generate.restype = _L
+lib.tlh_session_init.argtypes = [_P, _I]
+lib.tlh_session_init.restype = _I
+lib.tlh_run_prompt.argtypes = [_P, _P, _P, _I, _I, _I, _P, _P, _P, _L]
+lib.tlh_run_prompt.restype = _L
 lib.tlh_gpu_attn_ops_create.argtypes = [_I, _I, _I, _I, _I, _F, _I]
 lib.tlh_gpu_attn_ops_create.restype = _P
 lib.tlh_gpu_attn_ops_destroy.argtypes = [_P]
@@ -72,6 +76,34 @@ class Model:
                              buf.ctypes.data_as(C.c_void_p) if dump else None, cap)
         if n < 0:
             raise RuntimeError(lib.tlh_last_error().decode())
+        return ids, gaps, buf[:n] if dump else None
+
+    @staticmethod
+    def session_init(ops, n_new: int) -> None:
+        """initKvCache(max(32, nNew + 32)) of the REPL (src/tinylama.nim:47): the cache that
+        the following run_prompt calls share."""
+        if lib.tlh_session_init(ops, n_new) != 0:
+            raise RuntimeError(lib.tlh_last_error().decode())
+
+    def run_prompt(self, ops, prompt, n_new: int, chunked: bool = False, dump: bool = True):
+        """runPrompt (src/tinylama.nim:49-86) for one REPL line on the session's cache: the
+        first line is prefilled, a later one is fed through forwardDecode token by token, or
+        with chunked=True in one pass at positions curLen.. (tables with prefill_at).  Returns
+        greedy ids, top-2 gaps and the attention outputs in call order."""
+        hp = self.hp
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(n_new, np.int32)
+        gaps = np.zeros(n_new, np.float32)
+        hd = hp.nEmb // hp.nHead
+        cap = hp.nLayer * hp.nHead * hd * (len(prompt) + n_new) if dump else 0
+        buf = np.zeros(max(cap, 1), np.float32)
+        n = lib.tlh_run_prompt(self.h, ops, prompt.ctypes.data_as(C.c_void_p), len(prompt), n_new,
+                               1 if chunked else 0, ids.ctypes.data_as(C.c_void_p),
+                               gaps.ctypes.data_as(C.c_void_p),
+                               buf.ctypes.data_as(C.c_void_p) if dump else None, cap)
+        if n < 0:
+            msg = lib.tlh_last_error().decode()
+            raise (ValueError if "KV cache full" in msg else RuntimeError)(msg)
         return ids, gaps, buf[:n] if dump else None
 
     def close(self):
