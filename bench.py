@@ -392,38 +392,51 @@ def kernel_device_ms(fn, reps: int = 3) -> dict:
     return out
 
 
-def prefill_point(S: int, steps: int, warmup: int, dist, B=8, Hq=32, Hkv=8, D=64, kvd=1):
+def prefill_point(S: int, steps: int, warmup: int, dist, B=8, Hq=32, Hkv=8, D=64, kvd=1, start=0):
     """Causal prefill of B sequences of S tokens, sharded over the ranks (B/N each): RoPE + bf16
-    cache write + attention (tl_prefill_step).  Returns the step time (ms, max over ranks), the
-    device times of the attention kernel and of the RoPE/cache-write prologue (ms, max over
-    ranks), and the whole job's flops."""
+    cache write + attention (tl_prefill_step).  With start > 0 the S tokens continue a cached
+    prefix of `start` positions (tl_prefill_step_at: token t at start + t attends positions
+    0..start+t).  Returns the step time (ms, max over ranks), the device times of the attention
+    kernel and of the RoPE/cache-write prologue (ms, max over ranks), and the whole job's flops."""
     import torch
     from tinylama_b200 import _lib
     n = dist.world
     Bl = max(1, B // n)
     h = C.c_void_p()
-    _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, 10000.0, S, Bl, kvd,
+    _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, D, 10000.0, start + S, Bl, kvd,
                                        torch.cuda.current_device()))
     try:
         stream = torch.cuda.Stream()
         torch.cuda.set_stream(stream)
         g = torch.Generator(device="cuda").manual_seed(S * 16 + dist.rank)
+        p = lambda t: C.c_void_p(t.data_ptr())
+        sp = C.c_void_p(stream.cuda_stream)
+        for b in range(Bl if start > 0 else 0):  # the cached prefix (seeded N(0,1) K/V)
+            kp = torch.randn(start, Hkv * D, device="cuda", generator=g)
+            vp = torch.randn(start, Hkv * D, device="cuda", generator=g)
+            _lib.check(_lib.lib.tl_kv_store(h, 0, b, 0, p(kp), p(vp), start, sp))
+            del kp, vp
+        pos0_host = np.full(Bl, start, np.int32)
+        pos0 = torch.from_numpy(pos0_host).cuda()
         q = torch.randn(Bl, S, Hq * D, device="cuda", generator=g)
         k = torch.randn(Bl, S, Hkv * D, device="cuda", generator=g)
         v = torch.randn(Bl, S, Hkv * D, device="cuda", generator=g)
         out = torch.empty_like(q)
-        p = lambda t: C.c_void_p(t.data_ptr())
-        sp = C.c_void_p(stream.cuda_stream)
 
         def step():
-            _lib.check(_lib.lib.tl_prefill_step(h, 0, 0, Bl, S, p(q), p(k), p(v), p(out), sp))
+            if start > 0:
+                _lib.check(_lib.lib.tl_prefill_step_at(h, 0, 0, Bl, S, p(pos0), pos0_host.ctypes.data_as(C.c_void_p),
+                                                       p(q), p(k), p(v), p(out), sp))
+            else:
+                _lib.check(_lib.lib.tl_prefill_step(h, 0, 0, Bl, S, p(q), p(k), p(v), p(out), sp))
 
         ms = time_steps(step, steps, warmup, stream, dist)
         _lib.check(_lib.lib.tl_check_device(h, C.c_void_p(stream.cuda_stream)))
         kt = kernel_device_ms(step)
         core = sum(t for name, t in kt.items() if "prefill_tc_kernel" in name or "prefill_f32_kernel" in name)
         pro = sum(t for name, t in kt.items() if "rope_append" in name)
-        flops = Bl * n * Hq * 2 * D * S * (S + 1)
+        # 4*D flops per (query, key) pair; query t attends start + t + 1 keys
+        flops = Bl * n * Hq * 2 * D * (S * (S + 1) + 2 * S * start)
         return ms, dist.max(core), dist.max(pro), flops
     finally:
         _lib.lib.tl_attn_destroy(h)
@@ -433,12 +446,16 @@ def run_prefill(args, dist):
     sizes = [int(x) for x in args.prefill_sizes.split(",")]
     pk = peaks()
     res = {}
-    for S in sizes:
-        ms, core_ms, pro_ms, flops = prefill_point(S, max(5, args.steps // 2), args.warmup, dist)
+    points = [(0, S) for S in sizes]
+    for spec in filter(None, args.prefill_continue.split(",")):
+        start, S = (int(x) for x in spec.split(":"))
+        points.append((start, S))
+    for start, S in points:
+        ms, core_ms, pro_ms, flops = prefill_point(S, max(5, args.steps // 2), args.warmup, dist, start=start)
         tf = flops / (ms / 1e3) / 1e12
         tf_core = flops / (core_ms / 1e3) / 1e12 if core_ms > 0 else None
         peak = pk["bf16_tflops"] * dist.world  # whole job: N GPUs
-        res[str(S)] = {"ms_per_step": round(ms, 4), "tflops": round(tf, 1),
+        res[str(S) if start == 0 else f"{S} after {start} cached"] = {"ms_per_step": round(ms, 4), "tflops": round(tf, 1),
                        "frac_of_bf16_peak": round(tf / peak, 4), "flops": flops,
                        "attention_core": {"ms": round(core_ms, 4),
                                           "tflops": None if tf_core is None else round(tf_core, 1),
@@ -447,7 +464,8 @@ def run_prefill(args, dist):
                        "prologue_ms": round(pro_ms, 4)}
     return {"workload": "causal prefill, 8 sequences (sharded over the GPUs), 32 q / 8 kv heads, head_dim 64, "
                         "bf16 KV (tcgen05); step = RoPE + cache write + attention (end to end on the device); "
-                        "attention_core = the attention kernel alone (CUPTI device time)",
+                        "attention_core = the attention kernel alone (CUPTI device time); \"S after P cached\" = "
+                        "S new tokens continuing a cached prefix of P positions (tl_prefill_step_at)",
             "n_gpus": dist.world, "by_seq_len": res, "peak_tflops_per_gpu": pk["bf16_tflops"], "peak_src": pk["src"]}
 
 
@@ -636,6 +654,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the prefill sub-measurement")
     ap.add_argument("--prefill-sizes", default="512,2048,8192", help="sequence lengths of the prefill")
+    ap.add_argument("--prefill-continue", default="6144:2048",
+                    help="start:S points of a prefill continuing a cached prefix (comma-separated; empty: none)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (256 = the benchmark)")
     args = ap.parse_args()
