@@ -362,6 +362,7 @@ def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
     if not args.no_prefill and not gqa:
         res["prefill"] = run_prefill(args, dist)
         res["decode_tinyllama"] = run_decode_tiny(args, dist)
+        res["model_decode"] = run_model_decode(args, dist)
     if n == 1 and dist.rank == 0 and not args.no_cpu_baseline and not gqa:
         rate, sample = cpu_decode_sample(w.lens, w.Hq, w.Hkv, w.D, w.base, args.cpu_budget, 1)
         res["cpu_baseline"] = {"value": round(rate, 3), "unit": "tok/s", "cores": 1, "kind": "port",
@@ -467,6 +468,94 @@ def run_prefill(args, dist):
                         "attention_core = the attention kernel alone (CUPTI device time); \"S after P cached\" = "
                         "S new tokens continuing a cached prefix of P positions (tl_prefill_step_at)",
             "n_gpus": dist.world, "by_seq_len": res, "peak_tflops_per_gpu": pk["bf16_tflops"], "peak_src": pk["src"]}
+
+
+# ------------------------------------------------------- the whole model on the GPU (tl_model.h)
+def synthetic_q2k(rng, rows: int, cols: int) -> np.ndarray:
+    """Q2_K blocks of random content with the format's layout: 16 scale bytes, 64 bytes of 2-bit
+    weights, f16 d and dmin (positive, of the size N(0, 0.02) weights quantise to)."""
+    nb = rows * (cols // 256)
+    blk = rng.integers(0, 256, size=(nb, 84), dtype=np.uint8)
+    dd = (rng.random((nb, 2), dtype=np.float32) * np.float32(0.004) + np.float32(0.001)).astype(np.float16)
+    blk[:, 80:84] = dd.view(np.uint8).reshape(nb, 4)
+    return blk
+
+
+def run_model_decode(args, dist, n_prompt=8, n_new=129):
+    """TinyLlama-1.1B shapes (22 layers, dim 2048, 32/4 heads, ffn 5632, vocab 32000), Q2_K
+    matrices including the output, f32 embedding and norms, random synthetic weights: greedy
+    decode at batch 1 through tl_model_generate.  Each decode step is one CUDA graph replay
+    (embedding, per layer rmsnorm+qkv, RoPE+append+attention, wo+residual, rmsnorm+gate/up+silu,
+    down+residual, then rmsnorm+output and argmax); the device time of the n_new-1 steps comes
+    from CUDA events around them.  Bytes per step: every weight once (Q2_K 84 B per 256)."""
+    import torch
+    from tinylama_b200 import _lib
+    nL, E, H, KV, F, V, D = 22, 2048, 32, 4, 5632, 32000, 64
+    rng = np.random.default_rng(2026)
+
+    class Cfg(C.Structure):
+        _fields_ = [("nVocab", C.c_int), ("nEmb", C.c_int), ("nLayer", C.c_int), ("nFfn", C.c_int),
+                    ("nHead", C.c_int), ("nHeadKv", C.c_int), ("ropeDim", C.c_int),
+                    ("ropeFreqBase", C.c_float), ("rmsEps", C.c_float), ("maxLen", C.c_int)]
+
+    h = C.c_void_p()
+    _lib.check(_lib.lib.tl_model_create(C.byref(h), C.byref(Cfg(V, E, nL, F, H, KV, D, 10000.0, 1e-5, n_prompt + n_new)),
+                                        torch.cuda.current_device()))
+    try:
+        q2k_bytes = 0
+
+        def put(name, typ, arr, ne0, ne1):
+            _lib.check(_lib.lib.tl_model_set_tensor(h, name.encode(), typ, arr.ctypes.data_as(C.c_void_p), ne0, ne1))
+
+        ones = np.ones(E, np.float32)
+        for l in range(nL):
+            p = f"blk.{l}."
+            put(p + "attn_norm.weight", 0, ones, E, 1)
+            put(p + "ffn_norm.weight", 0, ones, E, 1)
+            for name, ne0, ne1 in (("attn_q", E, H * D), ("attn_k", E, KV * D), ("attn_v", E, KV * D),
+                                   ("attn_output", H * D, E), ("ffn_gate", E, F), ("ffn_up", E, F),
+                                   ("ffn_down", F, E)):
+                w = synthetic_q2k(rng, ne1, ne0)
+                q2k_bytes += w.nbytes
+                put(p + name + ".weight", 10, w, ne0, ne1)
+        put("output_norm.weight", 0, ones, E, 1)
+        w = synthetic_q2k(rng, V, E)
+        q2k_bytes += w.nbytes
+        put("output.weight", 10, w, E, V)
+        emb = (rng.standard_normal((V, E), dtype=np.float32) * np.float32(0.02))
+        put("token_embd.weight", 0, emb, E, V)
+        del emb, w
+        prompt = rng.integers(3, V, size=n_prompt).astype(np.int32)
+        ids = np.zeros(n_new, np.int32)
+        gaps = np.zeros(n_new, np.float32)
+
+        def gen():
+            _lib.check(_lib.lib.tl_model_generate(h, prompt.ctypes.data_as(C.c_void_p), n_prompt, n_new,
+                                                  ids.ctypes.data_as(C.c_void_p), gaps.ctypes.data_as(C.c_void_p)))
+
+        gen()  # captures the decode-step graph
+        per_step, e2e = [], []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            gen()
+            e2e.append(time.perf_counter() - t0)
+            pre, dec = C.c_float(), C.c_float()
+            _lib.check(_lib.lib.tl_model_last_timing(h, C.byref(pre), C.byref(dec)))
+            per_step.append(dec.value / (n_new - 1))
+        ms = statistics.median(per_step)
+        step_bytes = q2k_bytes + E * 4 * (2 * nL + 2)  # weights + embedding row + norm vectors
+        pk = peaks()
+        gbs = step_bytes / (ms / 1e3) / 1e9
+        return {"workload": "TinyLlama-1.1B shapes, Q2_K weights resident in HBM (random synthetic), greedy decode "
+                            "at batch 1, one CUDA graph per step (tl_model_generate)",
+                "prompt": n_prompt, "decode_steps": n_new - 1, "us_per_decode_step": round(ms * 1e3, 1),
+                "tok_s": round(1e3 / ms, 1), "bytes_per_step": step_bytes, "hbm_gbs": round(gbs, 1),
+                "frac_of_hbm_peak": round(gbs / pk["hbm_gbs"], 4), "peak_src": pk["src"],
+                "prefill_ms": round(pre.value, 3),
+                "e2e_tok_s": round(n_new / statistics.median(e2e), 1),
+                "e2e_note": "tl_model_generate wall clock: prompt upload, prefill, the decode steps, ids back"}
+    finally:
+        _lib.lib.tl_model_destroy(h)
 
 
 # ------------------------------------------------------------- TinyLlama decode latency
@@ -650,7 +739,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_batched",
                     choices=["decode_batched", "decode_batched_bf16", "decode_batched_gqa",
-                             "decode_batched_gqa_bf16", "splitkv", "prefill", "decode_tiny"])
+                             "decode_batched_gqa_bf16", "splitkv", "prefill", "decode_tiny", "model_decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the prefill sub-measurement")
     ap.add_argument("--prefill-sizes", default="512,2048,8192", help="sequence lengths of the prefill")
@@ -680,6 +769,8 @@ def main():
             res = run_splitkv(args, dist)
         elif args.workload == "decode_tiny":
             res = run_decode_tiny(args, dist)
+        elif args.workload == "model_decode":
+            res = run_model_decode(args, dist)
         else:
             res = run_prefill(args, dist)
         if dist.rank == 0:

@@ -97,6 +97,11 @@ TLH_API int tlh_session_init(tlh_attn_ops *ops, int nNew);
 TLH_API long tlh_run_prompt(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int nPrompt, int nNew,
                             int chunked, int32_t *outIds, float *gaps, float *attnOut, long attnCap);
 
+/* Upload every tensor of a loaded model to a GPU model (tl_model.h): Q2_K tensors as stored in
+ * the file, the others as the float32 the loader produced.  0 or a negative status. */
+struct tl_model;
+TLH_API int tlh_model_to_gpu(const tlh_model *m, struct tl_model *g);
+
 /* The attention procs on the B200 (libtlattn.so, one cache slot, f32 cache); the table has
  * prefill_at (tl_prefill_layer_at_host). */
 TLH_API tlh_attn_ops *tlh_gpu_attn_ops_create(int nLayer, int nHead, int nHeadKv, int headDim,

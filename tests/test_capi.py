@@ -1,5 +1,5 @@
 """The C-ABI library without a GPU: it loads, and it exports every function include/tl_attn.h
-declares (no compute calls)."""
+and include/tl_model.h declare (no compute calls)."""
 import ctypes
 import os
 import re
@@ -7,14 +7,16 @@ import re
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "tl_attn.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("tl_attn.h", "tl_model.h")]
 LIB = os.path.join(ROOT, "tinylama_b200", "libtlattn.so")
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(tl_[a-z0-9_]+)\s*\(", text)))
+    names = set()
+    for header in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(header).read(), flags=re.S)
+        names.update(re.findall(r"\b(tl_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 @pytest.fixture(scope="module")

@@ -113,3 +113,32 @@ def test_tinyllama_repl_lines_chunked(tinyllama):
         assert off == dump_o.size
     print(f"\nREPL ids {[r[0].tolist() for r in runs['oracle']]}; chunked attention normwise {worst:.2e}")
     assert worst <= 1e-3, worst
+
+
+def test_tinyllama_whole_model_on_gpu(tinyllama):
+    """The whole forward pass on the B200 (tl_model.h: Q2_K weights resident in HBM, the decode
+    steps replayed from a CUDA graph) against the reference-equivalent pipeline (C++ host
+    linears in float32, the oracle's attention): the same 8-token prompt and 16 greedy ids."""
+    import time
+    m = tinyllama
+    prompt = np.random.default_rng(SEED).integers(3, 32000, size=8).astype(np.int32)
+    ops_o = ora.lib().ora_attn_ops_create(m.hp.nLayer, m.hp.nHeadKv, m.hp.nEmb // m.hp.nHead)
+    try:
+        t0 = time.perf_counter()
+        ids_o, gaps_o, _ = m.generate(ops_o, prompt, 16, dump=False)
+        cpu_s = time.perf_counter() - t0
+    finally:
+        ora.lib().ora_attn_ops_destroy(ops_o)
+    g = m.to_gpu(max_len=48)
+    try:
+        ids_g, gaps_g = g.generate(prompt, 16)
+        ids_g2, _ = g.generate(prompt, 16)
+        pre_ms, dec_ms = g.last_timing()
+    finally:
+        g.close()
+    print(f"\nwhole model on the GPU: ids {ids_g.tolist()}; prefill {pre_ms:.3f} ms, "
+          f"{dec_ms / 15 * 1e3:.1f} us per decode step; CPU pipeline {cpu_s:.2f} s for 24 tokens; "
+          f"largest gap difference {float(np.max(np.abs(gaps_g - gaps_o))):.2e}")
+    assert np.array_equal(ids_g, ids_g2)
+    assert np.array_equal(ids_g, ids_o), (ids_g, ids_o, gaps_o)
+    assert float(np.max(np.abs(gaps_g - gaps_o))) <= 1e-2 * max(1.0, float(np.max(np.abs(gaps_o))))

@@ -63,6 +63,13 @@ SIGNATURES = {
     "tl_dist_init": (_I, [_P, _P, _I, _I]),
     "tl_decode_attention_dist": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "tl_dist_finalize": (None, [_P]),
+    # include/tl_model.h
+    "tl_model_create": (_I, [_P, _P, _I]),
+    "tl_model_destroy": (None, [_P]),
+    "tl_model_set_tensor": (_I, [_P, C.c_char_p, _I, _P, C.c_longlong, C.c_longlong]),
+    "tl_model_generate": (_I, [_P, _P, _I, _I, _P, _P]),
+    "tl_model_last_logits": (_I, [_P, _P]),
+    "tl_model_last_timing": (_I, [_P, _P, _P]),
 }
 
 if not os.path.exists(LIB_PATH):

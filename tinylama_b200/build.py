@@ -20,12 +20,13 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include")]
 SOURCES = ["tl_attn_api.cu", "rope_append.cu", "decode_attn.cu", "prefill_simt.cu",
-           "prefill_tc.cu", "dist.cu", "decode_noalloc.cu", "decode_mma.cu"]
+           "prefill_tc.cu", "dist.cu", "decode_noalloc.cu", "decode_mma.cu", "model_gpu.cu"]
 
 
 def _headers() -> list[str]:
     hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     hs.append(os.path.join(ROOT, "include", "tl_attn.h"))
+    hs.append(os.path.join(ROOT, "include", "tl_model.h"))
     return hs
 
 
@@ -54,7 +55,8 @@ CXX = os.environ.get("CXX", "g++")
 def build_host() -> str:
     """libtlhost.so: the C++ host forward pass (CPU linears) over libtlattn.so's attention.
     -ffp-contract=off keeps the reference's float32 rounding (no fused multiply-adds)."""
-    deps = [HOST_SRC, os.path.join(ROOT, "include", "tl_host.h"), os.path.join(ROOT, "include", "tl_attn.h"), LIB]
+    deps = [HOST_SRC, os.path.join(ROOT, "include", "tl_host.h"), os.path.join(ROOT, "include", "tl_attn.h"),
+            os.path.join(ROOT, "include", "tl_model.h"), LIB]
     if os.path.exists(HOST_LIB) and os.path.getmtime(HOST_LIB) >= max(os.path.getmtime(d) for d in deps):
         return HOST_LIB
     cmd = [CXX, "-O2", "-ffp-contract=off", "-fno-fast-math", "-std=c++17", "-fPIC", "-shared", "-pthread",

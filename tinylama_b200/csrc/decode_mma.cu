@@ -335,6 +335,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     if constexpr (CLU) cluster_sync_all();
     // launched behind the RoPE/append kernel: positions, q and the cache are read after it
     pdl_wait();
+    // a kernel launched behind this one with programmatic serialisation may start its own
+    // independent prologue (it waits for this grid's completion before reading its output)
+    pdl_launch_dependents();
     int total_units = 0;
     Unit cu{};
     if constexpr (!CLU) {

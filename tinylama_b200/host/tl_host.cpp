@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "../../include/tl_attn.h"
+#include "../../include/tl_model.h"
 
 namespace {
 
@@ -248,6 +249,12 @@ struct tlh_model {
     tlh_hparams hp{};
     std::string arch;
     std::map<std::string, Tensor> w;
+    // the Q2_K tensors as stored in the file, for the GPU model (which keeps them quantised)
+    struct Raw {
+        int64_t ne0 = 0, ne1 = 0;
+        std::vector<uint8_t> bytes;
+    };
+    std::map<std::string, Raw> q2k;
     int nthreads = 1;
 };
 
@@ -641,6 +648,12 @@ tlh_model *tlh_model_load(const char *path, int nthreads, char *err, int errlen)
                 }
             }
         });
+        if (ti.type == 10) {
+            tlh_model::Raw &r = m->q2k[ti.name];
+            r.ne0 = ne0;
+            r.ne1 = rows;
+            r.bytes.assign(src, src + (size_t)(rowBytes * rows));
+        }
         m->w[ti.name] = std::move(t);
     }
     return m;
@@ -712,6 +725,21 @@ long tlh_run_prompt(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int 
         outIds[j] = next;
     }
     return dump.n;
+}
+
+int tlh_model_to_gpu(const tlh_model *m, tl_model *g) {
+    if (!m || !g) return fail(-1, "bad argument");
+    for (const auto &kv : m->w) {
+        const Tensor &t = kv.second;
+        const int64_t ne0 = t.shape.empty() ? 1 : t.shape[0];
+        const int64_t ne1 = ne0 > 0 ? (int64_t)t.data.size() / ne0 : 0;
+        auto q = m->q2k.find(kv.first);
+        const int rc = q != m->q2k.end()
+                           ? tl_model_set_tensor(g, kv.first.c_str(), TL_GGML_Q2_K, q->second.bytes.data(), ne0, ne1)
+                           : tl_model_set_tensor(g, kv.first.c_str(), TL_GGML_F32, t.data.data(), ne0, ne1);
+        if (rc) return fail(rc, "%s", tl_last_error());
+    }
+    return 0;
 }
 
 tlh_attn_ops *tlh_gpu_attn_ops_create(int nLayer, int nHead, int nHeadKv, int headDim, int ropeDim, float base,

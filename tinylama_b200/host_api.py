@@ -35,6 +35,8 @@ lib.tlh_session_init.argtypes = [_P, _I]
 lib.tlh_session_init.restype = _I
 lib.tlh_run_prompt.argtypes = [_P, _P, _P, _I, _I, _I, _P, _P, _P, _L]
 lib.tlh_run_prompt.restype = _L
+lib.tlh_model_to_gpu.argtypes = [_P, _P]
+lib.tlh_model_to_gpu.restype = _I
 lib.tlh_gpu_attn_ops_create.argtypes = [_I, _I, _I, _I, _I, _F, _I]
 lib.tlh_gpu_attn_ops_create.restype = _P
 lib.tlh_gpu_attn_ops_destroy.argtypes = [_P]
@@ -106,6 +108,11 @@ class Model:
             raise (ValueError if "KV cache full" in msg else RuntimeError)(msg)
         return ids, gaps, buf[:n] if dump else None
 
+    def to_gpu(self, max_len: int, device: int = 0) -> "GpuModel":
+        """The whole forward pass on the B200 (include/tl_model.h) with this model's weights:
+        Q2_K tensors as stored in the file, the others as loaded float32."""
+        return GpuModel(self, max_len, device)
+
     def close(self):
         if self.h:
             lib.tlh_model_free(self.h)
@@ -127,3 +134,57 @@ def gpu_attn_ops(hp: HParams, device: int = 0):
 
 def free_gpu_attn_ops(ops) -> None:
     lib.tlh_gpu_attn_ops_destroy(ops)
+
+
+class TlModelConfig(C.Structure):
+    _fields_ = [("nVocab", _I), ("nEmb", _I), ("nLayer", _I), ("nFfn", _I), ("nHead", _I), ("nHeadKv", _I),
+                ("ropeDim", _I), ("ropeFreqBase", _F), ("rmsEps", _F), ("maxLen", _I)]
+
+
+class GpuModel:
+    """tl_model (include/tl_model.h): weights resident on the GPU, a greedy generation with one
+    CUDA graph replay per decode step."""
+
+    def __init__(self, model: Model, max_len: int, device: int = 0):
+        from tinylama_b200 import _lib
+        self._l = _lib
+        hp = model.hp
+        cfg = TlModelConfig(hp.nVocab, hp.nEmb, hp.nLayer, hp.nFfn, hp.nHead, hp.nHeadKv, hp.ropeDim,
+                            hp.ropeFreqBase, hp.rmsEps, max_len)
+        self.hp = hp
+        self.h = C.c_void_p()
+        _lib.check(_lib.lib.tl_model_create(C.byref(self.h), C.byref(cfg), device))
+        if lib.tlh_model_to_gpu(model.h, self.h) != 0:
+            msg = lib.tlh_last_error().decode()
+            self.close()
+            raise RuntimeError(msg)
+
+    def generate(self, prompt, n_new: int):
+        """runPrompt on the device: greedy ids and top-2 logit gaps."""
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(n_new, np.int32)
+        gaps = np.zeros(n_new, np.float32)
+        self._l.check(self._l.lib.tl_model_generate(self.h, prompt.ctypes.data_as(C.c_void_p), len(prompt), n_new,
+                                                    ids.ctypes.data_as(C.c_void_p), gaps.ctypes.data_as(C.c_void_p)))
+        return ids, gaps
+
+    def last_logits(self) -> np.ndarray:
+        out = np.empty(self.hp.nVocab, np.float32)
+        self._l.check(self._l.lib.tl_model_last_logits(self.h, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def last_timing(self) -> tuple[float, float]:
+        a, b = C.c_float(), C.c_float()
+        self._l.check(self._l.lib.tl_model_last_timing(self.h, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+    def close(self):
+        if self.h:
+            self._l.lib.tl_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
