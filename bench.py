@@ -543,6 +543,10 @@ def run_model_decode(args, dist, n_prompt=8, n_new=129):
             _lib.check(_lib.lib.tl_model_last_timing(h, C.byref(pre), C.byref(dec)))
             per_step.append(dec.value / (n_new - 1))
         ms = statistics.median(per_step)
+        # device time per kernel (CUPTI) of one generate call, per decode step: what the step's
+        # time is made of, and how much of it lies between kernels
+        kt = kernel_device_ms(gen, reps=1)
+        kernels = {k[:80]: round(v * 1e3 / n_new, 2) for k, v in sorted(kt.items(), key=lambda x: -x[1])[:8]}
         step_bytes = q2k_bytes + E * 4 * (2 * nL + 2)  # weights + embedding row + norm vectors
         pk = peaks()
         gbs = step_bytes / (ms / 1e3) / 1e9
@@ -552,6 +556,7 @@ def run_model_decode(args, dist, n_prompt=8, n_new=129):
                 "tok_s": round(1e3 / ms, 1), "bytes_per_step": step_bytes, "hbm_gbs": round(gbs, 1),
                 "frac_of_hbm_peak": round(gbs / pk["hbm_gbs"], 4), "peak_src": pk["src"],
                 "prefill_ms": round(pre.value, 3),
+                "kernel_us_per_step": kernels, "kernel_us_sum": round(sum(kt.values()) * 1e3 / n_new, 1),
                 "e2e_tok_s": round(n_new / statistics.median(e2e), 1),
                 "e2e_note": "tl_model_generate wall clock: prompt upload, prefill, the decode steps, ids back"}
     finally:

@@ -193,42 +193,80 @@ __device__ __forceinline__ void row_dot(const GMat &M, int row, int in, const fl
 }
 
 // The block's copy of x in shared memory: normalised (rmsnormCols) when a.norm is set, and the
-// sums of its 16-element sub-blocks.  Ends with a barrier.
+// sums of its 16-element sub-blocks.  Each thread loads its share of a token's x (and of the
+// norm weights) as float4s in one batch, so the row costs one round trip to L2, not one per
+// element.  V4 float4s per thread: inputs up to V4 * 1024 wide.  Ends with a barrier.
+constexpr int kMaxIn = 8192;
+constexpr int kV4 = kMaxIn / 4 / kThreads;  // float4s per thread at the widest input
+
+template <int V4>
 __device__ __forceinline__ void stage_x(const GemvArgs &a, float *xs, float *xsum, float *red) {
     const int xstride = xpad_len(a.in), sstride = a.in / 16;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n4 = a.in / 4;
     for (int s = 0; s < a.S; ++s) {
-        const float *xr = a.x + (size_t)s * a.in;
+        const float4 *xr = reinterpret_cast<const float4 *>(a.x + (size_t)s * a.in);
+        const float4 *wr = reinterpret_cast<const float4 *>(a.norm);
+        float4 v[V4], w[V4];
+#pragma unroll
+        for (int k = 0; k < V4; ++k) {
+            const int i4 = tid + k * kThreads;
+            if (i4 < n4) {
+                v[k] = xr[i4];
+                if (a.norm) w[k] = __ldg(wr + i4);
+            }
+        }
         float inv = 1.f;
         if (a.norm) {
             // rmsnormCols: inv = 1 / sqrt(sum x^2 / dim + eps); out = x * inv * w
             float ss = 0.f;
-            for (int i = tid; i < a.in; i += kThreads) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+            for (int k = 0; k < V4; ++k) {
+                if (tid + k * kThreads < n4) {
+                    ss = fmaf(v[k].x, v[k].x, ss);
+                    ss = fmaf(v[k].y, v[k].y, ss);
+                    ss = fmaf(v[k].z, v[k].z, ss);
+                    ss = fmaf(v[k].w, v[k].w, ss);
+                }
+            }
             ss = warp_sum(ss);
             if (lane == 0) red[warp] = ss;
             __syncthreads();
             if (warp == 0) {
-                float v = lane < kThreads / 32 ? red[lane] : 0.f;
-                v = warp_sum(v);
-                if (lane == 0) red[0] = v;
+                float t = lane < kThreads / 32 ? red[lane] : 0.f;
+                t = warp_sum(t);
+                if (lane == 0) red[0] = t;
             }
             __syncthreads();
             inv = 1.f / sqrtf(red[0] / (float)a.in + a.eps);
             __syncthreads();  // red is reused by the next token
         }
-        for (int i = tid; i < a.in; i += kThreads) {
-            const float v = a.norm ? __fmul_rn(__fmul_rn(xr[i], inv), a.norm[i]) : xr[i];
-            xs[s * xstride + xpad(i)] = v;
+#pragma unroll
+        for (int k = 0; k < V4; ++k) {
+            const int i4 = tid + k * kThreads;
+            if (i4 < n4) {
+                float4 o = v[k];
+                if (a.norm) {
+                    o.x = __fmul_rn(__fmul_rn(o.x, inv), w[k].x);
+                    o.y = __fmul_rn(__fmul_rn(o.y, inv), w[k].y);
+                    o.z = __fmul_rn(__fmul_rn(o.z, inv), w[k].z);
+                    o.w = __fmul_rn(__fmul_rn(o.w, inv), w[k].w);
+                }
+                *reinterpret_cast<float4 *>(xs + s * xstride + xpad(4 * i4)) = o;
+            }
         }
     }
     __syncthreads();
     for (int e = tid; e < a.S * sstride; e += kThreads) {
         const int s = e / sstride, j = e - s * sstride;
-        const float *p = xs + s * xstride + xpad(16 * j);  // 16 floats never cross a pad
-        float v = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v += p[i];
-        xsum[s * sstride + j] = v;
+        const float4 *p = reinterpret_cast<const float4 *>(xs + s * xstride + xpad(16 * j));  // no pad inside
+        const float4 p0 = p[0], p1 = p[1], p2 = p[2], p3 = p[3];
+        float t = p0.x;
+        t += p0.y; t += p0.z; t += p0.w;
+        t += p1.x; t += p1.y; t += p1.z; t += p1.w;
+        t += p2.x; t += p2.y; t += p2.z; t += p2.w;
+        t += p3.x; t += p3.y; t += p3.z; t += p3.w;
+        xsum[s * sstride + j] = t;
     }
     __syncthreads();
 }
@@ -241,7 +279,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvArgs a) {
     float *xsum = sm + NS * xstride;    // [NS][in/16]
     __shared__ float red[kThreads / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    stage_x(a, xs, xsum, red);
+    stage_x<kV4>(a, xs, xsum, red);
     // ---- rows: a warp per row task ----
     const int rows0 = a.m[0].rows;
     const int tasks = a.mode == kSwiGLU ? rows0 : rows0 + (a.nmat > 1 ? a.m[1].rows : 0) + (a.nmat > 2 ? a.m[2].rows : 0);
@@ -287,13 +325,34 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvArgs a) {
     }
 }
 
-// Q2_K matrices only, launched with programmatic dependent launch.  A warp's rows are software
-// pipelined: the quantised data of its next row (TPL quarters per lane: in / 2048 rounded up) is
-// loaded while the current one is computed, and the first row's is loaded before the kernel
-// waits for the previous one -- the weights depend on nothing, so their fetch overlaps the tail
-// of the kernel before.  SWI: gate and up rows together, silu(gate) * up out.
-template <int NS, int TPL, bool SWI>
-__global__ void __launch_bounds__(kThreads, 2) gemv_q2k_kernel(const GemvArgs a) {
+// RoPE and the cache append folded into the q/k/v product of a decode step (S = 1): a warp
+// computes rows 2i and 2i+1 of a head together, rotates q and k at the token's position like
+// applyRopeAtPos (src/forward.nim:125-139), writes q for the attention and k, v straight into
+// the f32 cache (storeKVRange, :232-241).
+struct RopeFuse {
+    const float *theta;  // [pairs] per-pair frequencies
+    int pairs, hd, layer;
+    const int *pos;      // device: the token's position
+    float *kc, *vc;      // the cache
+    KvLayout kv;
+    unsigned *err;
+};
+
+// Q2_K matrices only, launched with programmatic dependent launch.  Before the kernel waits for
+// the one before it, each warp loads the quantised data of its first PRE row tasks into
+// registers -- the weights depend on nothing, so their fetch overlaps the tail of the previous
+// kernel; later tasks are loaded PRE ahead of their use.  A task is RP consecutive rows (2 for
+// the RoPE pairs).  SWI: gate and up rows together, silu(gate) * up out.
+template <int NS, int TPL, bool SWI, int RP>
+struct Q2Cfg {
+    static constexpr int PER = RP * TPL * (SWI ? 2 : 1);  // Q2Part per task and lane
+    static constexpr int PRE = PER * 7 * 3 <= 48 ? 3 : (PER * 7 * 2 <= 48 ? 2 : 1);
+};
+
+template <int NS, int TPL, bool SWI, int RP>
+__global__ void __launch_bounds__(kThreads, 2) gemv_q2k_kernel(const GemvArgs a, const RopeFuse rf) {
+    using Cf = Q2Cfg<NS, TPL, SWI, RP>;
+    constexpr int PRE = Cf::PRE;
     extern __shared__ float sm[];
     const int xstride = xpad_len(a.in), sstride = a.in / 16;
     float *xs = sm;
@@ -303,90 +362,132 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q2k_kernel(const GemvArgs a)
     const int nb = a.in / QK, ntask = nb * 4;
     const size_t rowBytes = (size_t)nb * Q2K_BYTES;
     const int rows0 = a.m[0].rows;
-    const int tasks = SWI ? rows0 : rows0 + (a.nmat > 1 ? a.m[1].rows : 0) + (a.nmat > 2 ? a.m[2].rows : 0);
+    const int rowsAll = SWI ? rows0 : rows0 + (a.nmat > 1 ? a.m[1].rows : 0) + (a.nmat > 2 ? a.m[2].rows : 0);
+    const int tasks = rowsAll / RP;
     const int gw = blockIdx.x * (kThreads / 32) + warp, nw = gridDim.x * (kThreads / 32);
-    // task -> (matrix, row), without indexing the parameter array
-    auto locate = [&](int task, GMat &M, int &row) {
-        row = task;
+    const int count = gw < tasks ? (tasks - gw + nw - 1) / nw : 0;  // tasks of this warp
+    // task -> (matrix, first row), without indexing the parameter array
+    auto locate = [&](int task, GMat &M, int &row, int &mi) {
+        row = task * RP;
         M = a.m[0];
+        mi = 0;
         if (!SWI && a.nmat > 1 && row >= a.m[0].rows) {
             row -= a.m[0].rows;
             M = a.m[1];
+            mi = 1;
             if (a.nmat > 2 && row >= a.m[1].rows) {
                 row -= a.m[1].rows;
                 M = a.m[2];
+                mi = 2;
             }
         }
     };
-    auto load_row = [&](Q2Part (&P)[TPL], const uint8_t *R) {
+    auto load_task = [&](Q2Part (&P)[Cf::PER], int task) {
+        GMat M;
+        int row, mi;
+        locate(task, M, row, mi);
 #pragma unroll
-        for (int k = 0; k < TPL; ++k) {
-            const int t = lane + 32 * k;
-            if (t < ntask) q2_load(P[k], R + (size_t)(t >> 2) * Q2K_BYTES, (t >> 1) & 1, t & 1);
+        for (int r = 0; r < RP; ++r) {
+#pragma unroll
+            for (int k = 0; k < TPL; ++k) {
+                const int t = lane + 32 * k;
+                if (t < ntask) {
+                    const size_t off = (size_t)(row + r) * rowBytes + (size_t)(t >> 2) * Q2K_BYTES;
+                    q2_load(P[r * TPL + k], static_cast<const uint8_t *>(M.w) + off, (t >> 1) & 1, t & 1);
+                    if (SWI) q2_load(P[RP * TPL + r * TPL + k], static_cast<const uint8_t *>(a.m[1].w) + off, (t >> 1) & 1, t & 1);
+                }
+            }
         }
     };
-    Q2Part cur[TPL], curU[TPL], nxt[TPL], nxtU[TPL];
-    int task = gw;
-    if (task < tasks) {
-        GMat M;
-        int row;
-        locate(task, M, row);
-        load_row(cur, static_cast<const uint8_t *>(M.w) + row * rowBytes);
-        if (SWI) load_row(curU, static_cast<const uint8_t *>(a.m[1].w) + row * rowBytes);
-    }
+    Q2Part buf[PRE][Cf::PER];
+#pragma unroll
+    for (int j = 0; j < PRE; ++j)
+        if (j < count) load_task(buf[j], gw + j * nw);
     pdl_launch_dependents();  // the next kernel may start fetching its own weights
     pdl_wait();               // x comes from the kernel before
-    stage_x(a, xs, xsum, red);
-    while (task < tasks) {
-        const int next = task + nw;
-        if (next < tasks) {
-            GMat M;
-            int row;
-            locate(next, M, row);
-            load_row(nxt, static_cast<const uint8_t *>(M.w) + row * rowBytes);
-            if (SWI) load_row(nxtU, static_cast<const uint8_t *>(a.m[1].w) + row * rowBytes);
-        }
-        GMat M;
-        int row;
-        locate(task, M, row);
-        float acc[NS], up[NS];
+    stage_x<2 * TPL>(a, xs, xsum, red);
+    int pos = 0;
+    if (RP == 2 && rf.pos) pos = *rf.pos;
+    for (int j0 = 0; j0 < count; j0 += PRE) {
 #pragma unroll
-        for (int s = 0; s < NS; ++s) acc[s] = up[s] = 0.f;
+        for (int jj = 0; jj < PRE; ++jj) {
+            const int j = j0 + jj;
+            if (j >= count) break;
+            const int task = gw + j * nw;
+            float acc[RP][NS], up[RP][NS];
 #pragma unroll
-        for (int k = 0; k < TPL; ++k) {
-            const int t = lane + 32 * k;
-            if (t < ntask) {
-                q2_compute<NS>(cur[k], (t >> 1) & 1, t & 1, xs, xstride, xsum, sstride, (t >> 2) * QK, a.S, acc);
-                if (SWI) q2_compute<NS>(curU[k], (t >> 1) & 1, t & 1, xs, xstride, xsum, sstride, (t >> 2) * QK, a.S, up);
+            for (int r = 0; r < RP; ++r)
+#pragma unroll
+                for (int s = 0; s < NS; ++s) acc[r][s] = up[r][s] = 0.f;
+#pragma unroll
+            for (int r = 0; r < RP; ++r) {
+#pragma unroll
+                for (int k = 0; k < TPL; ++k) {
+                    const int t = lane + 32 * k;
+                    if (t < ntask) {
+                        const int n = (t >> 1) & 1, h = t & 1, base = (t >> 2) * QK;
+                        q2_compute<NS>(buf[jj][r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, acc[r]);
+                        if (SWI) q2_compute<NS>(buf[jj][RP * TPL + r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, up[r]);
+                    }
+                }
             }
-        }
+            // this slot is free: fetch the task PRE ahead into it
+            if (j + PRE < count) load_task(buf[jj], task + PRE * nw);
 #pragma unroll
-        for (int s = 0; s < NS; ++s) {
-            acc[s] = warp_sum(acc[s]);
-            if (SWI) up[s] = warp_sum(up[s]);
-        }
-        if (lane == 0) {
+            for (int r = 0; r < RP; ++r)
 #pragma unroll
-            for (int s = 0; s < NS; ++s) {
-                if (s < a.S) {
-                    if (SWI) {
-                        // silu(g) = g / (1 + exp(-g)) (src/tensor.nim:52-56), times up
-                        const float g = acc[s];
-                        const float sl = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
-                        M.y[(size_t)s * rows0 + row] = __fmul_rn(sl, up[s]);
-                    } else {
-                        float *dst = M.y + (size_t)s * M.rows + row;
-                        *dst = a.mode == kResidual ? __fadd_rn(*dst, acc[s]) : acc[s];
+                for (int s = 0; s < NS; ++s) {
+                    acc[r][s] = warp_sum(acc[r][s]);
+                    if (SWI) up[r][s] = warp_sum(up[r][s]);
+                }
+            if (lane != 0) continue;
+            GMat M;
+            int row, mi;
+            locate(task, M, row, mi);
+            if (RP == 2 && rf.pos) {
+                // decode step: rows (row, row+1) are a RoPE pair of head row / hd
+                float y0 = acc[0][0], y1 = acc[RP - 1][0];
+                const int head = row / rf.hd, d = row - head * rf.hd;
+                if (mi < 2 && (d >> 1) < rf.pairs) {
+                    const float angle = __fmul_rn((float)pos, rf.theta[d >> 1]);
+                    double sd, cd;
+                    sincos((double)angle, &sd, &cd);
+                    const float c = (float)cd, sn = (float)sd;
+                    const float r0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
+                    const float r1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
+                    y0 = r0;
+                    y1 = r1;
+                }
+                if (mi == 0) {
+                    M.y[row] = y0;
+                    M.y[row + 1] = y1;
+                } else if (pos >= 0 && pos < rf.kv.maxLen) {
+                    float *dst = (mi == 1 ? rf.kc : rf.vc) + rf.kv.row(rf.layer, 0, head, pos) * rf.hd + d;
+                    dst[0] = y0;
+                    dst[1] = y1;
+                } else if (rf.err) {
+                    atomicOr(rf.err, TL_DEVERR_POS_RANGE);
+                }
+                continue;
+            }
+#pragma unroll
+            for (int r = 0; r < RP; ++r) {
+#pragma unroll
+                for (int s = 0; s < NS; ++s) {
+                    if (s < a.S) {
+                        if (SWI) {
+                            // silu(g) = g / (1 + exp(-g)) (src/tensor.nim:52-56), times up
+                            const float g = acc[r][s];
+                            const float sl = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
+                            M.y[(size_t)s * rows0 + row + r] = __fmul_rn(sl, up[r][s]);
+                        } else {
+                            float *dst = M.y + (size_t)s * M.rows + row + r;
+                            *dst = a.mode == kResidual ? __fadd_rn(*dst, acc[r][s]) : acc[r][s];
+                        }
                     }
                 }
             }
         }
-#pragma unroll
-        for (int k = 0; k < TPL; ++k) {
-            cur[k] = nxt[k];
-            if (SWI) curU[k] = nxtU[k];
-        }
-        task = next;
     }
 }
 
@@ -500,6 +601,8 @@ struct tl_model {
     cudaGraphExec_t graphExec = nullptr;
     cudaEvent_t ev[3] = {};
     float prefillMs = 0.f, decodeMs = 0.f;
+    float *ropeTheta = nullptr;  // per-pair RoPE frequencies (device), for the fused decode q/k/v
+    int ropePairs = 0;
 };
 
 namespace {
@@ -558,8 +661,9 @@ int need(const tl_model *m, const GTensor **out, const std::string &name, int64_
 }
 
 int launch_gemv(tl_model *m, int mode, const GTensor *const *W, int nmat, float *const *y, const float *x, int S,
-                const float *norm) {
+                const float *norm, const RopeFuse *rope = nullptr) {
     const int in = (int)W[0]->ne0;
+    if (in > kMaxIn || in % 4 != 0) return api_fail(TL_ERR_UNSUPPORTED, "tl_model: matrix inputs wider than 8192");
     for (int s0 = 0; s0 < S; s0 += kMaxS) {
         GemvArgs a{};
         a.nmat = nmat;
@@ -577,18 +681,29 @@ int launch_gemv(tl_model *m, int mode, const GTensor *const *W, int nmat, float 
             a.m[i].y = y[i] + (size_t)s0 * W[i]->ne1;
             if (mode != kSwiGLU || i == 0) tasks += a.m[i].rows;
         }
+        if (rope) tasks /= 2;  // a warp takes a RoPE pair of rows
         const int blocks = std::max(1, std::min((tasks + 7) / 8, 2 * m->numSms));
         bool q2 = in % QK == 0 && in <= 4 * 2048;
         for (int i = 0; i < nmat; ++i) q2 = q2 && W[i]->type == TL_GGML_Q2_K;
         const int tpl = (in + 2047) / 2048;
         const bool swi = mode == kSwiGLU;
         const size_t smem = (size_t)(a.S == 1 ? 1 : kMaxS) * (xpad_len(in) + in / 16) * sizeof(float);
+        if (rope && !(q2 && S == 1)) return api_fail(TL_ERR_UNSUPPORTED, "fused RoPE needs Q2_K q/k/v and one token");
         if (q2) {
             cudaError_t e = cudaErrorInvalidValue;
-#define TLM_Q2(NS_, T_)                                                                                \
-    e = swi ? launch_pdl(gemv_q2k_kernel<NS_, T_, true>, dim3(blocks), dim3(kThreads), smem, m->stream, a) \
-            : launch_pdl(gemv_q2k_kernel<NS_, T_, false>, dim3(blocks), dim3(kThreads), smem, m->stream, a)
-            if (a.S == 1) {
+            const RopeFuse rf = rope ? *rope : RopeFuse{};
+#define TLM_Q2(NS_, T_)                                                                                         \
+    e = swi ? launch_pdl(gemv_q2k_kernel<NS_, T_, true, 1>, dim3(blocks), dim3(kThreads), smem, m->stream, a, rf) \
+            : launch_pdl(gemv_q2k_kernel<NS_, T_, false, 1>, dim3(blocks), dim3(kThreads), smem, m->stream, a, rf)
+#define TLM_Q2R(T_) e = launch_pdl(gemv_q2k_kernel<1, T_, false, 2>, dim3(blocks), dim3(kThreads), smem, m->stream, a, rf)
+            if (rope) {
+                switch (tpl) {
+                    case 1: TLM_Q2R(1); break;
+                    case 2: TLM_Q2R(2); break;
+                    case 3: TLM_Q2R(3); break;
+                    default: TLM_Q2R(4); break;
+                }
+            } else if (a.S == 1) {
                 switch (tpl) {
                     case 1: TLM_Q2(1, 1); break;
                     case 2: TLM_Q2(1, 2); break;
@@ -604,6 +719,7 @@ int launch_gemv(tl_model *m, int mode, const GTensor *const *W, int nmat, float 
                 }
             }
 #undef TLM_Q2
+#undef TLM_Q2R
             TLM_CUDA(e);
         } else if (a.S == 1) {
             gemv_kernel<1><<<blocks, kThreads, smem, m->stream>>>(a);
@@ -665,10 +781,28 @@ int forward(tl_model *m, const std::vector<LayerW> &L, const GTensor *emb, const
         const LayerW &w = L[l];
         const GTensor *qkv[3] = {w.wq, w.wk, w.wv};
         float *qkvy[3] = {m->q, m->k, m->v};
-        TLM_TRY(launch_gemv(m, kPlain, qkv, 3, qkvy, m->x, S, static_cast<const float *>(w.an->dev)));
-        if (decode) {
+        const bool fuse = decode && w.wq->type == TL_GGML_Q2_K && w.wk->type == TL_GGML_Q2_K &&
+                          w.wv->type == TL_GGML_Q2_K && m->ropeTheta != nullptr;
+        if (fuse) {
+            // q/k/v with RoPE at the step's position and k, v written into the cache; then the
+            // attention alone (src/forward.nim:314-317)
+            RopeFuse rf{};
+            rf.theta = m->ropeTheta;
+            rf.pairs = m->ropePairs;
+            rf.hd = hd;
+            rf.layer = l;
+            rf.pos = m->state + 1;
+            rf.kv = m->attn->kv;
+            rf.kc = static_cast<float *>(m->attn->kv.k);
+            rf.vc = static_cast<float *>(m->attn->kv.v);
+            rf.err = m->err;
+            TLM_TRY(launch_gemv(m, kPlain, qkv, 3, qkvy, m->x, 1, static_cast<const float *>(w.an->dev), &rf));
+            TLM_TRY(tl_decode_attention(m->attn, l, 0, 1, m->state + 1, nullptr, m->q, m->ctx, m->stream));
+        } else if (decode) {
+            TLM_TRY(launch_gemv(m, kPlain, qkv, 3, qkvy, m->x, S, static_cast<const float *>(w.an->dev)));
             TLM_TRY(tl_decode_step(m->attn, l, 0, 1, m->state + 1, nullptr, m->q, m->k, m->v, m->ctx, m->stream));
         } else {
+            TLM_TRY(launch_gemv(m, kPlain, qkv, 3, qkvy, m->x, S, static_cast<const float *>(w.an->dev)));
             TLM_TRY(tl_prefill_step(m->attn, l, 0, 1, S, m->q, m->k, m->v, m->ctx, m->stream));
         }
         const GTensor *wo[1] = {w.wo};
@@ -748,6 +882,8 @@ int tl_model_create(tl_model **out, const tl_model_config *cfg, int device) {
         return api_fail(TL_ERR_INVALID, "tl_model_create: sizes must be positive");
     if (c.nHead % c.nHeadKv != 0) return api_fail(TL_ERR_INVALID, "GQA requires head_count divisible by head_count_kv");
     if (c.nEmb % c.nHead != 0) return api_fail(TL_ERR_INVALID, "nEmb must be a multiple of nHead");
+    if (c.nEmb > kMaxIn || c.nFfn > kMaxIn)
+        return api_fail(TL_ERR_UNSUPPORTED, "tl_model: nEmb and nFfn up to 8192");
     if (c.nEmb % QK != 0 || c.nFfn % QK != 0)
         return api_fail(TL_ERR_UNSUPPORTED, "tl_model: nEmb and nFfn must be multiples of 256");
     tl_model *m = new tl_model();
@@ -769,6 +905,13 @@ int tl_model_create(tl_model **out, const tl_model_config *cfg, int device) {
     if (e == cudaSuccess) e = cudaMalloc(&m->err, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(m->err, 0, sizeof(unsigned));
     for (int i = 0; i < 3 && e == cudaSuccess; ++i) e = cudaEventCreate(&m->ev[i]);
+    if (e == cudaSuccess && ropeDim <= m->headDim && ropeDim % 2 == 0 && ropeDim / 2 <= kMaxRopePairs) {
+        const RopeTab tab = make_rope_tab(ropeDim, c.ropeFreqBase);  // the frequencies of the RoPE kernels
+        e = cudaMalloc(&m->ropeTheta, sizeof(float) * (tab.pairs > 0 ? tab.pairs : 1));
+        if (e == cudaSuccess && tab.pairs > 0)
+            e = cudaMemcpy(m->ropeTheta, tab.theta, sizeof(float) * tab.pairs, cudaMemcpyHostToDevice);
+        m->ropePairs = tab.pairs;
+    }
     // the largest gemv (kMaxS tokens of the ffn input) needs more than the default 48 KB
     const int big = std::max(c.nEmb, c.nFfn);
     const int smem = kMaxS * (xpad_len(big) + big / 16) * (int)sizeof(float);
@@ -778,10 +921,12 @@ int tl_model_create(tl_model **out, const tl_model_config *cfg, int device) {
                                  (xpad_len(big) + big / 16) * (int)sizeof(float));
     // the pipelined Q2_K kernels take inputs up to 8192 wide
     const int smem1 = (xpad_len(8192) + 8192 / 16) * (int)sizeof(float), smem4 = kMaxS * smem1;
-#define TLM_ATTR(NS_, T_, SW_)                                                                          \
-    if (e == cudaSuccess)                                                                              \
-        e = cudaFuncSetAttribute(gemv_q2k_kernel<NS_, T_, SW_>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 NS_ == 1 ? smem1 : smem4);
+#define TLM_ATTR(NS_, T_, SW_)                                                                             \
+    if (e == cudaSuccess)                                                                                 \
+        e = cudaFuncSetAttribute(gemv_q2k_kernel<NS_, T_, SW_, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 NS_ == 1 ? smem1 : smem4);                                              \
+    if (e == cudaSuccess && NS_ == 1 && !SW_)                                                            \
+        e = cudaFuncSetAttribute(gemv_q2k_kernel<1, T_, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1);
     TLM_ATTR(1, 1, false) TLM_ATTR(1, 2, false) TLM_ATTR(1, 3, false) TLM_ATTR(1, 4, false)
     TLM_ATTR(1, 1, true) TLM_ATTR(1, 2, true) TLM_ATTR(1, 3, true) TLM_ATTR(1, 4, true)
     TLM_ATTR(kMaxS, 1, false) TLM_ATTR(kMaxS, 2, false) TLM_ATTR(kMaxS, 3, false) TLM_ATTR(kMaxS, 4, false)
@@ -805,6 +950,7 @@ void tl_model_destroy(tl_model *m) {
     cudaFree(m->x); cudaFree(m->q); cudaFree(m->k); cudaFree(m->v); cudaFree(m->ctx); cudaFree(m->hb);
     cudaFree(m->logits); cudaFree(m->state); cudaFree(m->err); cudaFree(m->tokens); cudaFree(m->ids);
     cudaFree(m->gaps);
+    cudaFree(m->ropeTheta);
     for (auto &ev : m->ev)
         if (ev) cudaEventDestroy(ev);
     if (m->stream) cudaStreamDestroy(m->stream);
