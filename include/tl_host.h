@@ -69,6 +69,11 @@ typedef struct tlh_hparams {
  * (32-row chunks, src/forward.nim:51-74); 1 is the default build.  NULL on failure, with a
  * message in err. */
 TLH_API tlh_model *tlh_model_load(const char *path, int nthreads, char *err, int errlen);
+/* The same file mapped read-only (mmap), with no float32 copy of the weights: for
+ * tlh_model_to_gpu, which uploads Q2_K and float32 tensors straight from the mapping (the
+ * gguf_loader.nim:327-331 view of the data, without model.nim:116-123's dequantised cache).
+ * tlh_model_tensor dequantises on demand; the CPU forward pass refuses such a model. */
+TLH_API tlh_model *tlh_model_open(const char *path, char *err, int errlen);
 TLH_API void tlh_model_free(tlh_model *m);
 TLH_API int tlh_model_hparams(const tlh_model *m, tlh_hparams *out);
 /* Copy the dequantised float32 data of tensor `name` (getTensor, src/model.nim:116-123) into

@@ -133,6 +133,30 @@ def test_repl_lines_match_numpy(small_model):
         m.close()
 
 
+def test_mapped_open_keeps_no_float32_copy(small_model):
+    """tlh_model_open maps the file: the same hyper-parameters and (dequantised on demand) the
+    same tensors as tlh_model_load, and the CPU forward pass refuses it."""
+    from tinylama_b200.host_api import Model
+    path, keep = small_model
+    a = Model(path, nthreads=2)
+    b = Model(path, mapped=True)
+    try:
+        for f in ("nVocab", "nEmb", "nLayer", "nFfn", "nHead", "nHeadKv", "ropeDim"):
+            assert getattr(a.hp, f) == getattr(b.hp, f), f
+        for name in ("blk.0.attn_q.weight", "blk.1.ffn_down.weight", "output.weight", "token_embd.weight",
+                     "blk.0.attn_norm.weight"):
+            assert np.array_equal(a.tensor(name), b.tensor(name)), name
+        ops = ora.lib().ora_attn_ops_create(b.hp.nLayer, b.hp.nHeadKv, b.hp.nEmb // b.hp.nHead)
+        try:
+            with pytest.raises(RuntimeError, match="tlh_model_load"):
+                b.generate(ops, np.array([3, 4], np.int32), 2)
+        finally:
+            ora.lib().ora_attn_ops_destroy(ops)
+    finally:
+        a.close()
+        b.close()
+
+
 def test_forward_errors_follow_the_reference(small_model):
     from tinylama_b200 import host_api
     with pytest.raises(ValueError, match="cannot open"):

@@ -51,6 +51,26 @@ def test_generate_matches_numpy(small, n_prompt, n_new):
             break
 
 
+def test_mapped_file_uploads_the_same_model(small, tmp_path):
+    """Weights uploaded straight from the mapped GGUF (no float32 copy on the host) give the
+    same greedy ids and gaps as those from the loaded model."""
+    from tinylama_b200.host_api import Model
+    m, _ = small
+    path = str(tmp_path / "small.gguf")
+    gguf_synth.write_model(path, seed=7, **SMALL)
+    prompt = np.random.default_rng(4).integers(3, 512, size=6).astype(np.int32)
+    mm = Model(path, mapped=True)
+    g1, g2 = m.to_gpu(max_len=32), mm.to_gpu(max_len=32)
+    try:
+        ids1, gaps1 = g1.generate(prompt, 5)
+        ids2, gaps2 = g2.generate(prompt, 5)
+    finally:
+        g1.close()
+        g2.close()
+        mm.close()
+    assert np.array_equal(ids1, ids2) and np.array_equal(gaps1, gaps2)
+
+
 def test_logits_match_numpy(small):
     """The logits of the prefill's last token against the numpy forward."""
     m, npm = small

@@ -15,7 +15,11 @@
 // products and sums round as the reference's do.
 #include "../../include/tl_host.h"
 
+#include <fcntl.h>
 #include <math.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -255,7 +259,18 @@ struct tlh_model {
         std::vector<uint8_t> bytes;
     };
     std::map<std::string, Raw> q2k;
+    // tlh_model_open: the file mapped read-only and each tensor's place in it, no float32 copy
+    struct View {
+        int32_t type = 0;
+        int64_t ne0 = 0, rows = 0, rowBytes = 0;
+        std::vector<int64_t> shape;
+        const uint8_t *src = nullptr;
+    };
+    std::map<std::string, View> views;
+    void *map = nullptr;
+    size_t mapSize = 0;
     int nthreads = 1;
+    ~tlh_model();
 };
 
 namespace {
@@ -522,14 +537,51 @@ extern "C" {
 
 const char *tlh_last_error(void) { return g_err.c_str(); }
 
-tlh_model *tlh_model_load(const char *path, int nthreads, char *err, int errlen) {
+}  // extern "C"
+
+tlh_model::~tlh_model() {
+    if (map) munmap(map, mapSize);
+}
+
+namespace {
+
+// float32 of a mapped tensor, row by row (getTensor's dequantisation, model.nim:116-123).
+void dequant_view(const tlh_model::View &v, float *dst) {
+    for (int64_t r = 0; r < v.rows; ++r) {
+        const uint8_t *sp = v.src + (size_t)r * v.rowBytes;
+        float *d = dst + (size_t)r * v.ne0;
+        switch (v.type) {
+            case 0: memcpy(d, sp, (size_t)v.ne0 * 4); break;
+            case 1:
+                for (int64_t c = 0; c < v.ne0; ++c) {
+                    uint16_t hv;
+                    memcpy(&hv, sp + 2 * c, 2);
+                    d[c] = half_to_float(hv);
+                }
+                break;
+            case 10: dequant_q2k(sp, d, (int)v.ne0); break;
+            case 11: dequant_q3k(sp, d, (int)v.ne0); break;
+            case 14: dequant_q6k(sp, d, (int)v.ne0); break;
+            default: break;
+        }
+    }
+}
+
+// Parse a GGUF image (gguf_loader.nim:194-237, model.nim:50-103).  mapped: keep views of the
+// tensors in the image (which the caller keeps alive); otherwise dequantise every tensor to
+// float32 (model.nim:116-123) and keep the Q2_K ones as stored too.
+tlh_model *parse_gguf(const uint8_t *data, size_t size, bool mapped, int nthreads, char *err, int errlen) {
     auto bad = [&](const char *msg) -> tlh_model * {
         if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", msg);
         g_err = msg;
         return nullptr;
     };
-    std::vector<uint8_t> buf;
-    if (load_file(path, buf)) return bad(g_err.c_str());
+    struct {
+        const uint8_t *p;
+        size_t n;
+        const uint8_t *data() const { return p; }
+        size_t size() const { return n; }
+    } buf{data, size};
     Reader r{buf.data(), buf.size()};
     if (buf.size() < 4 || memcmp(buf.data(), "GGUF", 4) != 0) return bad("GGUF: invalid magic");
     r.pos = 4;
@@ -614,7 +666,6 @@ tlh_model *tlh_model_load(const char *path, int nthreads, char *err, int errlen)
         const int64_t rows = ne0 > 0 ? count / ne0 : 0;
         Tensor t;
         t.shape.assign(ti.ne, ti.ne + std::max<uint32_t>(ti.nDims, 1));
-        t.data.resize((size_t)count);
         const uint8_t *src = buf.data() + dataOffset + ti.offset;
         int64_t rowBytes = 0;
         void (*deq)(const uint8_t *, float *, int) = nullptr;
@@ -631,6 +682,17 @@ tlh_model *tlh_model_load(const char *path, int nthreads, char *err, int errlen)
             delete m;
             return bad("GGUF: tensor data offset out of range");
         }
+        if (mapped) {
+            tlh_model::View &v = m->views[ti.name];
+            v.type = ti.type;
+            v.ne0 = ne0;
+            v.rows = rows;
+            v.rowBytes = rowBytes;
+            v.shape = t.shape;
+            v.src = src;
+            continue;
+        }
+        t.data.resize((size_t)count);
         parallel_chunks((int)rows, 64, m->nthreads, [&](int s, int e) {
             for (int rr = s; rr < e; ++rr) {
                 float *dst = t.data.data() + (size_t)rr * ne0;
@@ -659,6 +721,45 @@ tlh_model *tlh_model_load(const char *path, int nthreads, char *err, int errlen)
     return m;
 }
 
+}  // namespace
+
+extern "C" {
+
+tlh_model *tlh_model_load(const char *path, int nthreads, char *err, int errlen) {
+    std::vector<uint8_t> buf;
+    if (load_file(path, buf)) {
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", g_err.c_str());
+        return nullptr;
+    }
+    return parse_gguf(buf.data(), buf.size(), false, nthreads, err, errlen);
+}
+
+tlh_model *tlh_model_open(const char *path, char *err, int errlen) {
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) {
+        fail(-1, "cannot open %s", path);
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", g_err.c_str());
+        return nullptr;
+    }
+    struct stat st;
+    void *p = MAP_FAILED;
+    if (fstat(fd, &st) == 0 && st.st_size > 0) p = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) {
+        fail(-1, "cannot map %s", path);
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", g_err.c_str());
+        return nullptr;
+    }
+    tlh_model *m = parse_gguf(static_cast<const uint8_t *>(p), (size_t)st.st_size, true, 1, err, errlen);
+    if (!m) {
+        munmap(p, (size_t)st.st_size);
+        return nullptr;
+    }
+    m->map = p;
+    m->mapSize = (size_t)st.st_size;
+    return m;
+}
+
 void tlh_model_free(tlh_model *m) { delete m; }
 
 int tlh_model_hparams(const tlh_model *m, tlh_hparams *out) {
@@ -669,6 +770,18 @@ int tlh_model_hparams(const tlh_model *m, tlh_hparams *out) {
 
 int tlh_model_tensor(const tlh_model *m, const char *name, float *out, long cap, long *n) {
     if (!m || !name) return fail(-1, "NULL argument");
+    if (m->map) {
+        auto v = m->views.find(name);
+        if (v == m->views.end()) return fail(-1, "missing tensor: %s", name);
+        const size_t count = (size_t)(v->second.ne0 * v->second.rows);
+        if (n) *n = (long)count;
+        if (out) {
+            std::vector<float> tmp(count);
+            dequant_view(v->second, tmp.data());
+            memcpy(out, tmp.data(), sizeof(float) * std::min<size_t>((size_t)cap, count));
+        }
+        return 0;
+    }
     auto it = m->w.find(name);
     if (it == m->w.end()) return fail(-1, "missing tensor: %s", name);
     if (n) *n = (long)it->second.data.size();
@@ -679,6 +792,7 @@ int tlh_model_tensor(const tlh_model *m, const char *name, float *out, long cap,
 long tlh_generate(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int nPrompt, int nNew, int32_t *outIds,
                   float *gaps, float *attnOut, long attnCap) {
     if (!m || !ops || !prompt || nPrompt <= 0 || nNew <= 0 || !outIds) return fail(-1, "bad argument");
+    if (m->map) return fail(-1, "a model opened with tlh_model_open has no float32 weights; the CPU forward pass needs tlh_model_load");
     int rc = ops->init_cache(ops->ctx, std::max(32, nNew + 32));  // src/tinylama.nim:47
     if (rc) return rc;
     Dump dump{attnOut, attnCap};
@@ -703,6 +817,7 @@ int tlh_session_init(tlh_attn_ops *ops, int nNew) {
 long tlh_run_prompt(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int nPrompt, int nNew, int chunked,
                     int32_t *outIds, float *gaps, float *attnOut, long attnCap) {
     if (!m || !ops || !prompt || nPrompt <= 0 || nNew <= 0 || !outIds) return fail(-1, "bad argument");
+    if (m->map) return fail(-1, "a model opened with tlh_model_open has no float32 weights; the CPU forward pass needs tlh_model_load");
     Dump dump{attnOut, attnCap};
     std::vector<int32_t> toks(prompt, prompt + nPrompt);
     Tensor logits;
@@ -729,6 +844,24 @@ long tlh_run_prompt(tlh_model *m, tlh_attn_ops *ops, const int32_t *prompt, int 
 
 int tlh_model_to_gpu(const tlh_model *m, tl_model *g) {
     if (!m || !g) return fail(-1, "bad argument");
+    if (m->map) {
+        // straight from the mapped file: Q2_K and float32 tensors as stored, the others
+        // dequantised one tensor at a time
+        for (const auto &kv : m->views) {
+            const tlh_model::View &v = kv.second;
+            int rc;
+            if (v.type == 10 || v.type == 0) {
+                rc = tl_model_set_tensor(g, kv.first.c_str(), v.type == 10 ? TL_GGML_Q2_K : TL_GGML_F32, v.src, v.ne0,
+                                         v.rows);
+            } else {
+                std::vector<float> tmp((size_t)(v.ne0 * v.rows));
+                dequant_view(v, tmp.data());
+                rc = tl_model_set_tensor(g, kv.first.c_str(), TL_GGML_F32, tmp.data(), v.ne0, v.rows);
+            }
+            if (rc) return fail(rc, "%s", tl_last_error());
+        }
+        return 0;
+    }
     for (const auto &kv : m->w) {
         const Tensor &t = kv.second;
         const int64_t ne0 = t.shape.empty() ? 1 : t.shape[0];

@@ -23,6 +23,8 @@ class HParams(C.Structure):
 lib = C.CDLL(LIB_PATH)
 lib.tlh_model_load.restype = _P
 lib.tlh_model_load.argtypes = [C.c_char_p, _I, C.c_char_p, _I]
+lib.tlh_model_open.restype = _P
+lib.tlh_model_open.argtypes = [C.c_char_p, C.c_char_p, _I]
 lib.tlh_model_free.argtypes = [_P]
 lib.tlh_model_free.restype = None
 lib.tlh_model_hparams.argtypes = [_P, C.POINTER(HParams)]
@@ -45,11 +47,15 @@ lib.tlh_last_error.restype = C.c_char_p
 
 
 class Model:
-    """loadModel (src/model.nim:105-114) with every tensor dequantised up front."""
+    """loadModel (src/model.nim:105-114) with every tensor dequantised up front, or with
+    mapped=True the file mapped without a float32 copy (for to_gpu only)."""
 
-    def __init__(self, path: str, nthreads: int = 1):
+    def __init__(self, path: str, nthreads: int = 1, mapped: bool = False):
         err = C.create_string_buffer(512)
-        self.h = lib.tlh_model_load(path.encode(), nthreads, err, 512)
+        if mapped:
+            self.h = lib.tlh_model_open(path.encode(), err, 512)
+        else:
+            self.h = lib.tlh_model_load(path.encode(), nthreads, err, 512)
         if not self.h:
             raise ValueError(err.value.decode())
         self.hp = HParams()
