@@ -774,7 +774,7 @@ int resolve(tl_model *m, std::vector<LayerW> &L, const GTensor **emb, const GTen
 int forward(tl_model *m, const std::vector<LayerW> &L, const GTensor *emb, const GTensor *onorm, const GTensor *out,
             int S, const int32_t *tokens, bool decode) {
     const tl_model_config &c = m->c;
-    const int hd = m->headDim, qd = c.nHead * hd, kvd = c.nHeadKv * hd;
+    const int hd = m->headDim;
     embed_kernel<<<S, 256, 0, m->stream>>>(emb->type, emb->dev, c.nVocab, c.nEmb, tokens, m->state, m->x, m->err);
     TLM_CUDA(cudaGetLastError());
     for (int l = 0; l < c.nLayer; ++l) {
@@ -813,8 +813,6 @@ int forward(tl_model *m, const std::vector<LayerW> &L, const GTensor *emb, const
         TLM_TRY(launch_gemv(m, kSwiGLU, gu, 2, hy, m->x, S, static_cast<const float *>(w.fn->dev)));
         const GTensor *wd[1] = {w.wd};
         TLM_TRY(launch_gemv(m, kResidual, wd, 1, xo, m->hb, S, nullptr));
-        (void)qd;
-        (void)kvd;
     }
     // linearOut of the last token only: argmaxLast reads the last column
     GTensor ow = *out;
