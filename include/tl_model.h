@@ -14,7 +14,8 @@
  * the argmax of one step feeds the next, so a greedy generation makes no host round trip per
  * token.  The KV cache is float32, like the reference's.
  *
- * Errors: TL_* codes of tl_attn.h, message from tl_last_error().
+ * Errors: TL_* codes of tl_attn.h, message from tl_last_error().  A model is bound to its
+ * device and stream and is not thread-safe; calls are synchronous.
  */
 #ifndef TL_MODEL_H
 #define TL_MODEL_H
@@ -47,7 +48,8 @@ TL_API void tl_model_destroy(tl_model *m);
 /* Upload one tensor under its GGUF name ("token_embd.weight", "blk.3.attn_q.weight",
  * "output_norm.weight", ...).  ne0 = the innermost (input) dimension, ne1 = rows (1 for a
  * vector).  data: ne1 rows of ne0 float32 (TL_GGML_F32), or of ne0/256 Q2_K blocks
- * (TL_GGML_Q2_K).  Copied; the caller keeps its buffer. */
+ * (TL_GGML_Q2_K).  Copied; the caller keeps its buffer.  Replacing a tensor drops the captured
+ * decode step (the next tl_model_generate captures it again). */
 TL_API int tl_model_set_tensor(tl_model *m, const char *name, int ggmlType, const void *data, long long ne0,
                                long long ne1);
 

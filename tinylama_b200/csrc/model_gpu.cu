@@ -969,8 +969,14 @@ int tl_model_set_tensor(tl_model *m, const char *name, int ggmlType, const void 
         return api_fail(TL_ERR_UNSUPPORTED, "tl_model_set_tensor: type must be F32 or Q2_K");
     }
     DevGuard g(m->device);
+    // the captured decode step holds the old tensors' addresses
+    if (m->graphExec) { cudaGraphExecDestroy(m->graphExec); m->graphExec = nullptr; }
+    if (m->graph) { cudaGraphDestroy(m->graph); m->graph = nullptr; }
     GTensor &t = m->w[name];
-    if (t.dev) cudaFree(t.dev);
+    if (t.dev) {
+        cudaStreamSynchronize(m->stream);  // no queued work may still read it
+        cudaFree(t.dev);
+    }
     t = GTensor{};
     void *p = nullptr;
     TLM_CUDA(cudaMalloc(&p, bytes));
@@ -1036,7 +1042,8 @@ int tl_model_generate(tl_model *m, const int32_t *prompt, int nPrompt, int nNew,
     if (word) {
         cudaMemsetAsync(m->err, 0, sizeof(unsigned), m->stream);
         cudaStreamSynchronize(m->stream);
-        return api_fail(TL_ERR_DEVICE, "tl_model: a token id outside the vocabulary reached the device");
+        return api_fail(TL_ERR_DEVICE, (word & kErrToken) ? "tl_model: a token id outside the vocabulary reached the device"
+                                                          : "tl_model: a position outside the KV cache reached the device");
     }
     return tl_check_device(m->attn, m->stream);
 }
