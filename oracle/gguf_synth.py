@@ -116,7 +116,8 @@ def _nbytes(ne, typ) -> int:
 
 def write_model(path: str, seed: int = 0, nLayer: int = 22, nEmb: int = 2048, nHead: int = 32,
                 nHeadKv: int = 4, nFfn: int = 5632, nVocab: int = 32000, ropeBase: float = 10000.0,
-                rmsEps: float = 1e-5, sigma: float = 0.02, nCtx: int = 2048, keep: dict | None = None) -> str:
+                rmsEps: float = 1e-5, sigma: float = 0.02, nCtx: int = 2048, keep: dict | None = None,
+                ropeDim: int = 0) -> str:
     """Write the synthetic model; tensors are generated and quantised one at a time.  When `keep`
     is a dict it receives every tensor's stored bytes (small models only)."""
     rng = np.random.default_rng(seed)
@@ -130,7 +131,7 @@ def write_model(path: str, seed: int = 0, nLayer: int = 22, nEmb: int = 2048, nH
         ("llama.feed_forward_length", GGUF_U32, nFfn),
         ("llama.attention.head_count", GGUF_U32, nHead),
         ("llama.attention.head_count_kv", GGUF_U32, nHeadKv),
-        ("llama.rope.dimension_count", GGUF_U32, nEmb // nHead),
+        ("llama.rope.dimension_count", GGUF_U32, ropeDim if ropeDim > 0 else nEmb // nHead),
         ("llama.rope.freq_base", GGUF_F32, ropeBase),
         ("llama.attention.layer_norm_rms_epsilon", GGUF_F32, rmsEps),
     ]

@@ -37,8 +37,9 @@ class NumpyModel:
             q = self.lin(xn, p + "attn_q.weight")
             k = self.lin(xn, p + "attn_k.weight")
             v = self.lin(xn, p + "attn_v.weight")
-            q = numpy_ref.rope_cols(q, nH, hd, hd, hp["base"], positions).astype(np.float32)
-            k = numpy_ref.rope_cols(k, nKv, hd, hd, hp["base"], positions).astype(np.float32)
+            rd = hp.get("ropeDim", hd)  # partial rotary: the first ropeDim dims of a head
+            q = numpy_ref.rope_cols(q, nH, hd, rd, hp["base"], positions).astype(np.float32)
+            k = numpy_ref.rope_cols(k, nKv, hd, rd, hp["base"], positions).astype(np.float32)
             kc[layer][:, pos0:pos0 + S] = k
             vc[layer][:, pos0:pos0 + S] = v
             ctx = numpy_ref.attention(q, kc[layer], vc[layer], nH, nKv, hd, positions, pos0 + S).astype(np.float32)

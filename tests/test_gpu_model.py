@@ -89,6 +89,37 @@ def test_logits_match_numpy(small):
     assert err <= 1e-4, err
 
 
+def test_partial_rotary_matches_numpy(tmp_path, cuda_lib):
+    """ropeDim < headDim (llama.rope.dimension_count = 32 of 64): the decode step's fused
+    q/k/v + RoPE rotates only the first 32 dims of each head, as applyRopeAtPos does."""
+    from tinylama_b200.host_api import Model
+    keep = {}
+    path = str(tmp_path / "rope32.gguf")
+    gguf_synth.write_model(path, seed=9, keep=keep, ropeDim=32, **SMALL)
+    t = {}
+    for name, (ne, typ, raw) in keep.items():
+        n = int(np.prod(ne))
+        a = np.frombuffer(raw, np.float32) if typ == 0 else gguf_synth.dequantize_q2k(raw, n)
+        t[name] = a.reshape(ne[::-1]) if len(ne) == 2 else a
+    npm = NumpyModel(t, dict(nLayer=2, nEmb=256, nHead=4, nHeadKv=2, base=10000.0, eps=1e-5, ropeDim=32))
+    m = Model(path, nthreads=2)
+    assert m.hp.ropeDim == 32
+    prompt = np.random.default_rng(5).integers(3, 512, size=5).astype(np.int32)
+    g = m.to_gpu(max_len=32)
+    try:
+        ids, gaps = g.generate(prompt, 6)
+    finally:
+        g.close()
+        m.close()
+    nids, ngaps, _ = npm.generate(prompt, 6, 32)
+    for j in range(6):
+        if ngaps[j] > 1e-3:
+            assert ids[j] == nids[j], (j, ids, nids, ngaps)
+            assert abs(gaps[j] - ngaps[j]) <= 1e-3 * max(1.0, abs(ngaps[j])), (j, gaps, ngaps)
+        else:
+            break
+
+
 def test_errors_follow_the_reference(small):
     m, _ = small
     g = m.to_gpu(max_len=10)
