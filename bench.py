@@ -761,6 +761,7 @@ def main():
                     help="start:S points of a prefill continuing a cached prefix (comma-separated; empty: none)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (256 = the benchmark)")
+    ap.add_argument("--ctx-len", type=int, default=131072, help="split-KV context length (131072 = the benchmark)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     dist = Dist()
@@ -780,7 +781,7 @@ def main():
         elif args.workload == "decode_batched_gqa_bf16":
             res = run_decode_batched(args, dist, 1, (32, 4, 64))
         elif args.workload == "splitkv":
-            res = run_splitkv(args, dist)
+            res = run_splitkv(args, dist, L=args.ctx_len)
         elif args.workload == "decode_tiny":
             res = run_decode_tiny(args, dist)
         elif args.workload == "model_decode":
