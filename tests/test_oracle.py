@@ -126,3 +126,37 @@ def test_golden_fixtures_reproduce():
     # and the fixtures agree with the independent restatement
     r = numpy_ref.attention(g["full_q"], g["full_k"], g["full_v"], Hq, Hkv, D, np.arange(8), 8)
     assert max_rel_err(g["full_ctx"], r) < 1e-4
+
+
+def test_attention_cached_ignores_columns_past_curlen():
+    """attentionCached reads columns j < curLen only (src/forward.nim:191-205): what the cache
+    holds past them cannot change ctx."""
+    rng = np.random.default_rng(12)
+    Hq, Hkv, D, L, cap = 8, 2, 64, 40, 64
+    kc, vc = randn(rng, Hkv * D, cap), randn(rng, Hkv * D, cap)
+    q = randn(rng, Hq * D, 1)
+    a = ora.attention_cached(q, kc, vc, L, Hq, Hkv, D)
+    kc[:, L:] = 1e4
+    vc[:, L:] = np.nan
+    b = ora.attention_cached(q, kc, vc, L, Hq, Hkv, D)
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,S", [(32, 4, 64, 9), (8, 8, 128, 5)])
+def test_prefill_equals_one_decode_step_per_token(Hq, Hkv, D, S):
+    """forwardPrefill's attention block over S tokens (RoPE over 0..S-1, store, attentionFull)
+    against S forwardDecode blocks (RoPE at t, store at t, attentionCached over t+1 columns):
+    the two procs do the same float32 arithmetic per query, so the columns agree exactly.  This
+    is the equivalence the REPL path relies on when it feeds a later line in one pass."""
+    rng = np.random.default_rng(S * 3 + D)
+    base = 10000.0
+    q, k, v = randn(rng, Hq * D, S), randn(rng, Hkv * D, S), randn(rng, Hkv * D, S)
+    qr = ora.rope_single(q, Hq, D, D, base)
+    kr = ora.rope_single(k, Hkv, D, D, base)
+    full = ora.attention_full_ctx(qr, kr, v, Hq, Hkv, D)
+    kc = np.zeros((Hkv * D, S), np.float32)
+    vc = np.zeros((Hkv * D, S), np.float32)
+    steps = [ora.decode_step(q[:, t:t + 1], k[:, t:t + 1], v[:, t:t + 1], kc, vc, t, Hq, Hkv, D, D, base)
+             for t in range(S)]
+    assert np.array_equal(kc, kr) and np.array_equal(vc, v)
+    assert np.array_equal(np.concatenate(steps, axis=1), full)
