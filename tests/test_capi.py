@@ -60,3 +60,19 @@ def test_create_fails_cleanly_without_gpu_or_with_bad_shape(built_lib):
     assert b"GQA requires head_count divisible by head_count_kv" in _lib.lib.tl_last_error()
     rc = _lib.lib.tl_attn_create(ctypes.byref(h), 1, 32, 4, 96, 96, 10000.0, 16, 1, 0, 0)
     assert rc == _lib.TL_ERR_UNSUPPORTED
+
+
+def test_model_create_checks_shapes_before_any_device_call(built_lib):
+    """tl_model_create refuses bad hyper-parameters with the reference's messages before it
+    touches a GPU (so these run here, without one)."""
+    from tinylama_b200 import _lib
+    from tinylama_b200.host_api import TlModelConfig
+    h = ctypes.c_void_p()
+    bad_gqa = TlModelConfig(512, 256, 2, 512, 6, 4, 64, 10000.0, 1e-5, 32)
+    assert _lib.lib.tl_model_create(ctypes.byref(h), ctypes.byref(bad_gqa), 0) == _lib.TL_ERR_INVALID
+    assert b"GQA requires head_count divisible by head_count_kv" in _lib.lib.tl_last_error()
+    odd_ffn = TlModelConfig(512, 256, 2, 500, 4, 2, 64, 10000.0, 1e-5, 32)
+    assert _lib.lib.tl_model_create(ctypes.byref(h), ctypes.byref(odd_ffn), 0) == _lib.TL_ERR_UNSUPPORTED
+    zero = TlModelConfig(512, 256, 0, 512, 4, 2, 64, 10000.0, 1e-5, 32)
+    assert _lib.lib.tl_model_create(ctypes.byref(h), ctypes.byref(zero), 0) == _lib.TL_ERR_INVALID
+    assert not h.value
