@@ -88,8 +88,9 @@ def _kv_bytes(key: str, typ: int, val) -> bytes:
     return out
 
 
-def tensor_plan(nLayer, nEmb, nHead, nHeadKv, nFfn, nVocab):
-    """(name, ne, ggml type) of every tensor, in file order."""
+def tensor_plan(nLayer, nEmb, nHead, nHeadKv, nFfn, nVocab, f32: tuple = ()):
+    """(name, ne, ggml type) of every tensor, in file order.  Matrices whose name ends with one
+    of the suffixes in `f32` are stored as float32 instead of Q2_K."""
     kvDim = nHeadKv * (nEmb // nHead)
     plan = [("token_embd.weight", (nEmb, nVocab), GGML_F32)]
     for i in range(nLayer):
@@ -106,7 +107,7 @@ def tensor_plan(nLayer, nEmb, nHead, nHeadKv, nFfn, nVocab):
             (p + "ffn_down.weight", (nFfn, nEmb), GGML_Q2K),
         ]
     plan += [("output_norm.weight", (nEmb,), GGML_F32), ("output.weight", (nEmb, nVocab), GGML_Q2K)]
-    return plan
+    return [(n, ne, GGML_F32 if any(n.endswith(sfx) for sfx in f32) else t) for n, ne, t in plan]
 
 
 def _nbytes(ne, typ) -> int:
@@ -117,7 +118,7 @@ def _nbytes(ne, typ) -> int:
 def write_model(path: str, seed: int = 0, nLayer: int = 22, nEmb: int = 2048, nHead: int = 32,
                 nHeadKv: int = 4, nFfn: int = 5632, nVocab: int = 32000, ropeBase: float = 10000.0,
                 rmsEps: float = 1e-5, sigma: float = 0.02, nCtx: int = 2048, keep: dict | None = None,
-                ropeDim: int = 0) -> str:
+                ropeDim: int = 0, f32: tuple = ()) -> str:
     """Write the synthetic model; tensors are generated and quantised one at a time.  When `keep`
     is a dict it receives every tensor's stored bytes (small models only)."""
     rng = np.random.default_rng(seed)
@@ -135,7 +136,7 @@ def write_model(path: str, seed: int = 0, nLayer: int = 22, nEmb: int = 2048, nH
         ("llama.rope.freq_base", GGUF_F32, ropeBase),
         ("llama.attention.layer_norm_rms_epsilon", GGUF_F32, rmsEps),
     ]
-    plan = tensor_plan(nLayer, nEmb, nHead, nHeadKv, nFfn, nVocab)
+    plan = tensor_plan(nLayer, nEmb, nHead, nHeadKv, nFfn, nVocab, f32)
     header = b"GGUF" + struct.pack("<IQQ", 3, len(plan), len(kvs))
     header += b"".join(_kv_bytes(*kv) for kv in kvs)
     offset = 0

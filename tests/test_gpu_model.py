@@ -120,6 +120,38 @@ def test_partial_rotary_matches_numpy(tmp_path, cuda_lib):
             break
 
 
+def test_float32_matrices_take_the_generic_kernel(tmp_path, cuda_lib):
+    """A model whose wo, ffn_down and output matrices are float32 (as a loader hands over any
+    type other than Q2_K): those products run in the generic kernel, the others in the Q2_K
+    one, and the result still matches numpy."""
+    from tinylama_b200.host_api import Model
+    keep = {}
+    path = str(tmp_path / "mixed.gguf")
+    gguf_synth.write_model(path, seed=13, keep=keep, f32=("attn_output.weight", "ffn_down.weight", "output.weight"),
+                           **SMALL)
+    t = {}
+    for name, (ne, typ, raw) in keep.items():
+        n = int(np.prod(ne))
+        a = np.frombuffer(raw, np.float32) if typ == 0 else gguf_synth.dequantize_q2k(raw, n)
+        t[name] = a.reshape(ne[::-1]) if len(ne) == 2 else a
+    npm = NumpyModel(t, dict(nLayer=2, nEmb=256, nHead=4, nHeadKv=2, base=10000.0, eps=1e-5))
+    m = Model(path, nthreads=2)
+    prompt = np.random.default_rng(6).integers(3, 512, size=6).astype(np.int32)
+    g = m.to_gpu(max_len=32)
+    try:
+        ids, gaps = g.generate(prompt, 5)
+    finally:
+        g.close()
+        m.close()
+    nids, ngaps, _ = npm.generate(prompt, 5, 32)
+    for j in range(5):
+        if ngaps[j] > 1e-3:
+            assert ids[j] == nids[j], (j, ids, nids, ngaps)
+            assert abs(gaps[j] - ngaps[j]) <= 1e-3 * max(1.0, abs(ngaps[j])), (j, gaps, ngaps)
+        else:
+            break
+
+
 def test_errors_follow_the_reference(small):
     m, _ = small
     g = m.to_gpu(max_len=10)
