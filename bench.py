@@ -319,7 +319,20 @@ def cpu_decode_sample(lens, Hq, Hkv, D, base, budget_s: float, threads: int, see
 
 
 # ------------------------------------------------------------------------------ workloads
-def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
+def decode_config(n: int, B: int, lens, Hq: int, Hkv: int, D: int, kvd: int) -> dict:
+    """The workload's config dict; the reference arm reports the same one."""
+    gqa = Hkv != Hq
+    kv_gb = float(np.sum(np.asarray(lens, np.int64) + 1)) * Hkv * D * 2 * (4 if kvd == 0 else 2) / 1e9
+    return {"workload": "batched multi-sequence decode (TinyLlama GQA attention)" if gqa else
+                        "batched multi-sequence decode (Llama-2-7B-style attention)",
+            "seqs_per_gpu": B, "global_batch": B * n, "ctx_len": "U[256,4096] seeded",
+            "mean_ctx": float(np.mean(lens)), "n_head": Hq, "n_head_kv": Hkv,
+            "head_dim": D, "kv_dtype": "f32" if kvd == 0 else "bf16",
+            "parallelism": f"batch-sharded x{n} (no collective)",
+            "l2": f"no flush: {kv_gb:.1f} GB of KV read per step >> 126 MB L2"}
+
+
+def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128), with_subs=True):
     import torch
     pk = peaks()
     Hq, Hkv, D = shape
@@ -333,7 +346,8 @@ def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
     n = dist.world
     value = n * w.B / (ms / 1e3)
     achieved = w.algorithmic_bytes_attention() / (ms_attn / 1e3) / 1e9
-    e2e_dt, h2d, d2h = w.e2e(max(3, args.steps // 4), 2, dist)
+    # end to end through the host-buffer call (the headline line only)
+    e2e_dt, h2d, d2h = w.e2e(max(3, args.steps // 4), 2, dist) if with_subs else (ms / 1e3, 0, 0)
     e2e_value = n * w.B / e2e_dt
     traffic = traffic_from_profiles(("decode_kernel_f32" if kvd == 0 else "decode_kernel_bf16") + ("_gqa" if gqa else ""),
                                     w.algorithmic_bytes_attention())
@@ -341,13 +355,7 @@ def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": n, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32" if kvd == 0 else "bf16-kv/f32-math", "data": "synthetic",
-        "config": {"workload": "batched multi-sequence decode (TinyLlama GQA attention)" if gqa else
-                               "batched multi-sequence decode (Llama-2-7B-style attention)",
-                   "seqs_per_gpu": w.B, "global_batch": w.B * n, "ctx_len": "U[256,4096] seeded",
-                   "mean_ctx": float(np.mean(w.lens)), "n_head": w.Hq, "n_head_kv": w.Hkv,
-                   "head_dim": w.D, "kv_dtype": "f32" if kvd == 0 else "bf16",
-                   "parallelism": f"batch-sharded x{n} (no collective)",
-                   "l2": f"no flush: {w.kv_bytes() / 1e9:.1f} GB of KV read per step >> 126 MB L2"},
+        "config": decode_config(n, w.B, w.lens, Hq, Hkv, D, kvd),
         "hbm_gbs_step": round(w.kv_bytes() / (ms / 1e3) / 1e9, 1),
         "clocks": clocks,
         "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
@@ -359,17 +367,54 @@ def run_decode_batched(args, dist, kvd: int, shape=(32, 32, 128)):
                      "algorithmic_bytes_per_launch": w.algorithmic_bytes_attention(),
                      "launch_ms": round(ms_attn, 4)},
     }
-    if not args.no_prefill and not gqa:
-        res["prefill"] = run_prefill(args, dist)
-        res["decode_tinyllama"] = run_decode_tiny(args, dist)
-        res["model_decode"] = run_model_decode(args, dist)
-    if n == 1 and dist.rank == 0 and not args.no_cpu_baseline and not gqa:
+    if n == 1 and dist.rank == 0 and not args.no_cpu_baseline and with_subs:
         rate, sample = cpu_decode_sample(w.lens, w.Hq, w.Hkv, w.D, w.base, args.cpu_budget, 1)
         res["cpu_baseline"] = {"value": round(rate, 3), "unit": "tok/s", "cores": 1, "kind": "port",
                                "sample": sample + "; Malebolgia on/off identical (attention has no "
                                                   "Malebolgia path, src/forward.nim:51-74)"}
     w.close()
+    if with_subs and not args.no_subs:
+        res["north_star"] = north_star_subs(args, dist)
     return res
+
+
+def north_star_subs(args, dist) -> dict:
+    """Every other measurement the target names, in one flat dict of numbers (kept short so
+    that it survives in a log tail).  Decode: attention-kernel GB/s and fraction of the HBM
+    peak (256 sequences per GPU, L ~ U[256, 4096]).  Prefill: TFLOP/s and fraction of the burst
+    bf16 peak, attention kernel alone ("core") and the whole step (RoPE + cache write +
+    attention), 8 sequences sharded over the GPUs.  Split-KV: one 131072-token context per
+    sequence (B = 4, 32/8/128, bf16) split over the N GPUs, microseconds per step and the
+    fraction of the HBM peak each GPU sustains (strong scaling: the work is fixed).  TinyLlama
+    batch-1 decode step (RoPE + append + attention, K/V from HBM) and the whole TinyLlama model
+    decode step on the GPU, in microseconds."""
+    pk = peaks()
+    out = {"n_gpus": dist.world}
+    for tag, kvd, shape in (("gqa_f32", 0, (32, 4, 64)), ("gqa_bf16", 1, (32, 4, 64)),
+                            ("llama2_bf16", 1, (32, 32, 128))):
+        r = run_decode_batched(args, dist, kvd, shape, with_subs=False)
+        out[f"{tag}_gbs"] = r["roofline"]["achieved"]
+        out[f"{tag}_frac"] = r["roofline"]["frac"]
+        if tag == "llama2_bf16":
+            out[f"{tag}_tok_s"] = r["value"]
+    if not args.no_prefill:
+        pre = run_prefill(args, dist)
+        for key, d in pre["by_seq_len"].items():
+            k = key.replace(" after ", "_after_").replace(" cached", "")
+            out[f"prefill_{k}_core_tflops"] = d["attention_core"]["tflops"]
+            out[f"prefill_{k}_core_frac"] = d["attention_core"]["frac_of_bf16_peak"]
+            out[f"prefill_{k}_step_frac"] = d["frac_of_bf16_peak"]
+    sk = run_splitkv(args, dist, L=args.ctx_len)
+    out["splitkv_131072_us"] = round(sk["ms_per_step"] * 1e3, 1)
+    out["splitkv_131072_frac_per_gpu"] = sk["roofline"]["frac"]
+    tiny = run_decode_tiny(args, dist)
+    for L, d in tiny["by_ctx_len"].items():
+        out[f"tinyllama_b1_us_L{L}"] = d["hbm_rotating_64"]["us_per_step"]
+    md = run_model_decode(args, dist)
+    out["model_decode_us"] = md["us_per_decode_step"]
+    out["model_decode_frac"] = md["frac_of_hbm_peak"]
+    out["peaks"] = f"HBM {pk['hbm_gbs']} GB/s, bf16 {pk['bf16_tflops']} TF/s ({pk['src']})"
+    return out
 
 
 # -------------------------------------------------------------------- prefill (tcgen05)
@@ -718,7 +763,7 @@ def run_reference(args, dist):
     host threads, rank 0 only, on a bounded sample of the same workload."""
     if dist.rank != 0:
         return None
-    B, Hq, Hkv, D, base = 256, 32, 32, 128, 10000.0
+    B, Hq, Hkv, D, base = args.seqs, 32, 32, 128, 10000.0
     threads = os.cpu_count() or 1
     lens = seq_lens(1000, B)
     # size each step so that the whole run stays within a couple of minutes
@@ -735,9 +780,7 @@ def run_reference(args, dist):
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * B / value, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "batched multi-sequence decode (Llama-2-7B-style attention)",
-                   "seqs_per_gpu": B, "ctx_len": "U[256,4096] seeded", "n_head": Hq, "n_head_kv": Hkv,
-                   "head_dim": D, "kv_dtype": "f32"},
+        "config": decode_config(dist.world, B, lens, Hq, Hkv, D, 0),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": f"per step: {sample}, {threads} threads; the reference (Nim) "
                                    "cannot be built here, this is its C restatement"},
@@ -756,6 +799,7 @@ def main():
                              "decode_batched_gqa_bf16", "splitkv", "prefill", "decode_tiny", "model_decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the prefill sub-measurement")
+    ap.add_argument("--no-subs", action="store_true", help="omit every sub-measurement (headline only)")
     ap.add_argument("--prefill-sizes", default="512,2048,8192", help="sequence lengths of the prefill")
     ap.add_argument("--prefill-continue", default="6144:2048",
                     help="start:S points of a prefill continuing a cached prefix (comma-separated; empty: none)")

@@ -192,14 +192,19 @@ TL_API int tl_check_device(tl_attn *h, void *stream);
  * allocation's latency and implicit synchronisation): the same split-KV decode attention as
  * tl_decode_attention, without a handle and without any allocation.  The caller passes q [nseq][nHead*headDim],
  * the cache K and V, each head-major [nseq][nHeadKv][maxLen][headDim] of f32 or bf16 with
- * RoPE already applied, positions pos_dev / pos_host (both required; sequence b attends
- * positions 0..pos[b]) and out [nseq][nHead*headDim], all on the current device; the call is
- * asynchronous on `stream`.  The kernel's scratch is a fixed 16 MiB array inside the
- * library, held by every GPU that loads it until exit: at most 65536 (sequence, kv-head)
- * pairs per call, larger calls are refused with TL_ERR_INVALID.  The first call on a device
- * looks the array up (cudaGetSymbolAddress) and should come before any stream capture.  All
- * calls share the array and clear what they use at their start, so calls that can overlap
- * on the GPU race and must not be issued. */
+ * RoPE already applied, positions pos_dev / pos_host (both required and equal: sequence b
+ * attends positions 0..pos[b]; the schedule is sized from pos_host) and out
+ * [nseq][nHead*headDim], all on the current device; the call is asynchronous on `stream`.
+ * The kernel's scratch is a fixed 16 MiB array inside the library, held by every GPU that
+ * loads it until exit: at most 65536 (sequence, kv-head) pairs per call, and at most as many
+ * sequences as the decode kernel's shared memory holds (8 bytes per sequence beside a fixed
+ * part, checked against the device's per-block limit: some 15000 to 22000 sequences,
+ * depending on the shape); larger calls are refused with TL_ERR_INVALID.  There is no
+ * handle, so a device-side refusal (pos_dev disagreeing with pos_host, a position past maxLen)
+ * cannot be reported through tl_check_device: instead every element of `out` is set to NaN.
+ * The first call on a device looks the array up (cudaGetSymbolAddress) and should come before
+ * any stream capture.  All calls share the array and clear what they use at their start, so
+ * calls that can overlap on the GPU race and must not be issued. */
 TL_API int tl_decode_attention_noalloc(const float *q, const void *k_cache, const void *v_cache,
                                        int kvDtype, int nHead, int nHeadKv, int headDim, int maxLen,
                                        int nseq, const int *pos_dev, const int *pos_host, float *out,
@@ -214,8 +219,18 @@ TL_API int tl_dist_unique_id(char *id128);
  * [rank*maxLen, (rank+1)*maxLen) of every sequence (its slice).  Every rank exports an exchange
  * buffer with CUDA IPC and maps every peer's; NCCL is used here only to pass the IPC handles.
  * If the peers cannot be mapped (or TL_DIST_NCCL=1 is set), the calls below exchange through
- * an NCCL all-gather instead. */
+ * an NCCL all-gather instead.  If some rank never joins, the call fails with TL_ERR_NCCL after
+ * TL_DIST_INIT_TIMEOUT_MS milliseconds (environment; default 120000) instead of waiting for
+ * ever.  TL_DIST_WAIT_MS (default 2000) bounds each wait of a split-KV call for a peer's
+ * values.  TL_DIST_FAULT_SILENT_PEER=1 (test only, one-rank groups) injects a second rank
+ * whose values never arrive, so that every call runs into that bound. */
 TL_API int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank);
+/* Collective, after a split-KV call failed on some rank (a peer's values did not arrive in
+ * time, reported by tl_check_device as a wait-timeout, or a rank skipped a call): waits for this
+ * rank's queued work and agrees on a fresh epoch with every rank, so that the next call reads
+ * none of the values left over from the failed one.  Every rank calls it, the same number of
+ * times; afterwards the calls give correct results again. */
+TL_API int tl_dist_resync(tl_attn *h);
 /* Collective: every rank makes the same sequence of calls.  Split-KV decode across the ranks:
  * every rank passes the same q [nseq][nHead*headDim] (already rotated) and global positions
  * pos_dev/pos_host (the query attends global positions 0..pos[b]); each rank attends its

@@ -7,8 +7,10 @@ import bench
 
 def test_reference_arm_line(monkeypatch):
     monkeypatch.setattr(bench, "cpu_decode_sample", lambda *a, **k: (123.0, "stub sample"))
-    args = argparse.Namespace(steps=2, warmup=1, gpus=1)
+    args = argparse.Namespace(steps=2, warmup=1, gpus=1, seqs=256)
     res = bench.run_reference(args, bench.Dist())
+    # the same config dict as the GPU arm's line (rank 0's sequence lengths)
+    assert res["config"] == bench.decode_config(1, 256, bench.seq_lens(1000, 256), 32, 32, 128, 0)
     assert res["impl"] == "reference"
     for key in ("metric", "value", "unit", "higher_is_better", "config", "cpu_baseline", "e2e"):
         assert key in res, key

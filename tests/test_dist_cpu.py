@@ -71,3 +71,45 @@ def test_splitkv_merge_two_gloo_ranks(tmp_path, ctx_len):
     tmp.spawn(_rank, args=(2, _free_port(), ctx_len, path), nprocs=2, join=True)
     ctx, ref = np.load(path)
     assert np.max(np.abs(ctx - ref)) / np.max(np.abs(ref)) < 1e-5
+
+
+def _rank_never_exchanges(rank, world, port, result_path):
+    """Rank 1 joins the group but never takes part in the exchange of partials.  Rank 0's
+    exchange must end with an error once the group's timeout has passed, not wait for ever --
+    the host-side counterpart of the bounded waits in the split-KV kernel."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    Hq, Hkv, D, ctx_len = 8, 2, 64, 64
+    rng = np.random.default_rng(3)
+    k = rng.standard_normal((Hkv * D, ctx_len), dtype=np.float32)
+    v = rng.standard_normal((Hkv * D, ctx_len), dtype=np.float32)
+    q = rng.standard_normal((Hq * D, 1), dtype=np.float32)
+    if rank == 1:
+        time.sleep(8)  # alive, but never exchanges; leaves after rank 0 has given up
+        return
+    mine = torch.from_numpy(local_partial(q, k, v, Hq, Hkv, D, 0, ctx_len // 2))
+    gathered = [torch.zeros_like(mine) for _ in range(world)]
+    t0 = time.perf_counter()
+    try:
+        dist.all_gather(gathered, mine)
+        outcome = "completed"
+    except RuntimeError as e:
+        outcome = "error: " + str(e).splitlines()[0][:200]
+    np.save(result_path, np.array([outcome, f"{time.perf_counter() - t0:.2f}"]))
+
+
+def test_splitkv_exchange_ends_in_an_error_when_a_rank_never_joins(tmp_path):
+    import time
+
+    import torch.multiprocessing as tmp
+    path = str(tmp_path / "res.npy")
+    t0 = time.perf_counter()
+    tmp.spawn(_rank_never_exchanges, args=(2, _free_port(), path), nprocs=2, join=True)
+    outcome, waited = np.load(path)
+    assert outcome.startswith("error"), outcome
+    assert float(waited) < 30.0 and time.perf_counter() - t0 < 120.0

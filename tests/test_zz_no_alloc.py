@@ -14,14 +14,22 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kvd", [0, 1])
-def test_noalloc_matches_handle_decode(cuda_lib, kvd):
+RAGGED = [1900, 37, 1024, 1, 700, 1333]  # several sequences need multiple chunks
+
+
+@pytest.mark.parametrize("kvd,Hq,Hkv,D,lens,maxLen", [
+    (0, 32, 8, 128, RAGGED, 2048),     # f32, G = 4: tensor-core kernel (tf32 split)
+    (1, 32, 8, 128, RAGGED, 2048),     # bf16: tensor-core kernel
+    (0, 32, 32, 128, RAGGED, 2048),    # f32, G = 1: CUDA-core kernel
+    # 64 x 8192 positions at 64/8/128: at the usual chunk of 1024 the partials (4096 units x
+    # 1040 floats) exceed the scratch, so the call raises the chunk length until they fit
+    (1, 64, 8, 128, [8192] * 64, 8192),
+])
+def test_noalloc_matches_handle_decode(cuda_lib, kvd, Hq, Hkv, D, lens, maxLen):
     import torch
     _lib = cuda_lib
     torch.cuda.set_device(0)
-    B, Hq, Hkv, D = 6, 32, 8, 128
-    lens = [1900, 37, 1024, 1, 700, 1333]  # ragged; several sequences need multiple chunks
-    maxLen = 2048
+    B = len(lens)
     g = torch.Generator(device="cuda").manual_seed(123 + kvd)
     kt = torch.randn(B, maxLen, Hkv * D, device="cuda", generator=g)
     vt = torch.randn(B, maxLen, Hkv * D, device="cuda", generator=g)
@@ -77,3 +85,39 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(cuda_lib):
     rc = _lib.lib.tl_decode_attention_noalloc(p(q), p(q), p(q), 0, 32, 8, 128, 4, 1, p(dpos),
                                               np.array([4], np.int32).ctypes.data_as(C.c_void_p), p(q), None)
     assert rc == _lib.TL_ERR_KV_FULL
+    # 40000 sequences x 1 kv-head fit the pairs limit but not the decode kernel's shared memory
+    # (8 bytes per sequence): refused before any launch
+    nseq = 40000
+    posn = np.zeros(nseq, np.int32)
+    rc = _lib.lib.tl_decode_attention_noalloc(p(q), p(q), p(q), 0, 1, 1, 128, 1, nseq, p(dpos),
+                                              posn.ctypes.data_as(C.c_void_p), p(q), None)
+    assert rc == _lib.TL_ERR_INVALID
+    assert b"shared memory" in _lib.lib.tl_last_error()
+
+
+def test_noalloc_refusal_on_the_device_gives_nan(cuda_lib):
+    """A position past maxLen given only on the device (pos_host is in range) is caught by the
+    kernel's bounds check; with no handle to report it through, the output is set to NaN.  The
+    next good call gives finite output again."""
+    import torch
+    _lib = cuda_lib
+    torch.cuda.set_device(0)
+    B, Hq, Hkv, D, maxLen = 2, 32, 8, 128, 512
+    g = torch.Generator(device="cuda").manual_seed(9)
+    kc = torch.randn(B, Hkv, maxLen, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, maxLen, D, device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn(B, Hq * D, device="cuda", generator=g)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    pos = np.array([100, 300], np.int32)
+    bad = torch.tensor([100, 5000], dtype=torch.int32, device="cuda")
+    good = torch.from_numpy(pos).cuda()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out = torch.zeros(B, Hq * D, device="cuda")
+    _lib.check(_lib.lib.tl_decode_attention_noalloc(p(q), p(kc), p(vc), 1, Hq, Hkv, D, maxLen, B, p(bad),
+                                                    pos.ctypes.data_as(C.c_void_p), p(out), stream))
+    torch.cuda.synchronize()
+    assert torch.isnan(out).all()
+    _lib.check(_lib.lib.tl_decode_attention_noalloc(p(q), p(kc), p(vc), 1, Hq, Hkv, D, maxLen, B, p(good),
+                                                    pos.ctypes.data_as(C.c_void_p), p(out), stream))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()

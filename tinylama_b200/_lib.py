@@ -61,6 +61,7 @@ SIGNATURES = {
     "tl_decode_attention_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "tl_dist_unique_id": (_I, [_P]),
     "tl_dist_init": (_I, [_P, _P, _I, _I]),
+    "tl_dist_resync": (_I, [_P]),
     "tl_decode_attention_dist": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "tl_dist_finalize": (None, [_P]),
     # include/tl_model.h

@@ -22,6 +22,8 @@
 #include <float.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "internal.h"
@@ -350,9 +352,14 @@ __global__ void lse_merge_kernel(const float *__restrict__ parts, int nparts, in
 }
 
 template <typename KV, int D, int G>
+size_t smem_t(int nseq) {
+    return DecCfg<KV, D, G>::smem_bytes(nseq) + 4 * (size_t)nseq;
+}
+
+template <typename KV, int D, int G>
 cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     using C = DecCfg<KV, D, G>;
-    const size_t smem = C::smem_bytes(a.nseq) + 4 * (size_t)a.nseq;
+    const size_t smem = smem_t<KV, D, G>(a.nseq);
     auto kern = decode_kernel<KV, D, G>;
     // set the shared-memory limit only when it grows, so that steady-state launches (and CUDA
     // graph capture of them) make no attribute calls
@@ -380,10 +387,10 @@ cudaError_t launch_g(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
 }
 
 template <typename KV, int D, int G>
-int occ_t() {
+int occ_t(int nseq) {
     using C = DecCfg<KV, D, G>;
     int n = 0;
-    const size_t smem = C::smem_bytes(256) + 4 * 256;
+    const size_t smem = smem_t<KV, D, G>(nseq);
     cudaFuncSetAttribute(decode_kernel<KV, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<KV, D, G>, C::THREADS, smem) != cudaSuccess) n = 1;
     return n < 1 ? 1 : n;
@@ -410,37 +417,35 @@ cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
     return cudaErrorNotSupported;
 }
 
-static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype);
+static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype, int nseq);
 
-int decode_ctas_per_sm(int headDim, int group, int dtype) {
-    if (decode_mma_covers(headDim, group, dtype)) {
-        static int mcache[16][2][2][9];
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev >= 0 && dev < 16 && group >= 1 && group <= 8) {
-            int &slot = mcache[dev][headDim == 128][dtype == TL_KV_F32][group];
-            if (slot == 0) slot = decode_mma_ctas_per_sm(headDim, group, dtype);
-            return slot;
-        }
-        return decode_mma_ctas_per_sm(headDim, group, dtype);
-    }
-    // occupancy of each kernel instance, queried once per process and device
-    static int cache[16][2][2][9];  // [device][headDim 64/128][dtype][group]
+// The CTAs of one launch must all be resident at once (the split-KV exchange waits on CTAs of
+// the same launch), and the shared memory of a launch grows with nseq: the occupancy is taken
+// at the launch's own size, rounded up to a power of two (at least 256 sequences).
+int decode_ctas_per_sm(int headDim, int group, int dtype, int nseq) {
+    int bucket = 256, lg = 0;
+    while (bucket < nseq && lg < 15) { bucket <<= 1; ++lg; }
+    if (bucket < nseq) bucket = nseq;
+    static int cache[16][2][2][9][16];  // [device][headDim 64/128][dtype][group][size bucket]
+    static std::mutex mu;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 16 || group < 1 || group > 8) return decode_ctas_per_sm_uncached(headDim, group, dtype);
-    int &slot = cache[dev][headDim == 128][dtype == TL_KV_BF16][group];
-    if (slot == 0) slot = decode_ctas_per_sm_uncached(headDim, group, dtype);
+    if (dev < 0 || dev >= 16 || group < 1 || group > 8 || bucket > (256 << 15))
+        return decode_ctas_per_sm_uncached(headDim, group, dtype, bucket);
+    std::lock_guard<std::mutex> lock(mu);
+    int &slot = cache[dev][headDim == 128][dtype == TL_KV_BF16][group][lg];
+    if (slot == 0) slot = decode_ctas_per_sm_uncached(headDim, group, dtype, bucket);
     return slot;
 }
 
-static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype) {
+static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype, int nseq) {
+    if (decode_mma_covers(headDim, group, dtype)) return decode_mma_ctas_per_sm(headDim, group, dtype, nseq);
 #define TL_OCC(KV, D)                                  \
     switch (group) {                                   \
-        case 1: return occ_t<KV, D, 1>();              \
-        case 2: return occ_t<KV, D, 2>();              \
-        case 4: return occ_t<KV, D, 4>();              \
-        case 8: return occ_t<KV, D, 8>();              \
+        case 1: return occ_t<KV, D, 1>(nseq);          \
+        case 2: return occ_t<KV, D, 2>(nseq);          \
+        case 4: return occ_t<KV, D, 4>(nseq);          \
+        case 8: return occ_t<KV, D, 8>(nseq);          \
         default: return 1;                             \
     }
     if (headDim == 64) {
@@ -450,6 +455,25 @@ static int decode_ctas_per_sm_uncached(int headDim, int group, int dtype) {
     }
 #undef TL_OCC
     return 1;
+}
+
+size_t decode_smem_bytes(int headDim, int group, int dtype, int nseq) {
+    if (decode_mma_covers(headDim, group, dtype)) return decode_mma_smem_bytes(headDim, group, dtype, nseq);
+#define TL_SMEM(KV, D)                                     \
+    switch (group) {                                       \
+        case 1: return smem_t<KV, D, 1>(nseq);             \
+        case 2: return smem_t<KV, D, 2>(nseq);             \
+        case 4: return smem_t<KV, D, 4>(nseq);             \
+        case 8: return smem_t<KV, D, 8>(nseq);             \
+        default: return 0;                                 \
+    }
+    if (headDim == 64) {
+        if (dtype == TL_KV_F32) { TL_SMEM(float, 64) } else { TL_SMEM(__nv_bfloat16, 64) }
+    } else if (headDim == 128) {
+        if (dtype == TL_KV_F32) { TL_SMEM(float, 128) } else { TL_SMEM(__nv_bfloat16, 128) }
+    }
+#undef TL_SMEM
+    return 0;
 }
 
 size_t decode_partial_floats(int total_units, int group, int headDim) {

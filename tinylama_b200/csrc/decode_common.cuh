@@ -176,14 +176,17 @@ __device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long lo
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-// Wait (bounded by TL_WAIT_NS from t0) until the word carries this call's epoch; epochs only
-// grow.  Returns the value, or 0 with *ok cleared (and the timeout bit set) on time-out.
-__device__ __forceinline__ float wait_word(const unsigned long long *p, unsigned epoch, uint64_t t0, bool *ok,
-                                           unsigned *err) {
-    unsigned long long w = ld_word_sys(p);
-    while ((int)((unsigned)(w >> 32) - epoch) < 0) {
+// Has the word reached this call's epoch?  Epochs only grow.
+__device__ __forceinline__ bool word_ready(unsigned long long w, unsigned epoch) {
+    return (int)((unsigned)(w >> 32) - epoch) >= 0;
+}
+// Re-read a word until it carries this call's epoch, bounded by wait_ns from t0.  Returns the
+// value, or 0 with *ok cleared (and the timeout bit set) on time-out.
+__device__ __forceinline__ float wait_word(const unsigned long long *p, unsigned long long w, unsigned epoch,
+                                           uint64_t t0, unsigned long long wait_ns, bool *ok, unsigned *err) {
+    while (!word_ready(w, epoch)) {
         if (!*ok) return 0.f;
-        if (globaltimer_ns() - t0 > TL_WAIT_NS) {
+        if (globaltimer_ns() - t0 > wait_ns) {
             atomicOr(err, TL_DEVERR_TIMEOUT);
             *ok = false;
             return 0.f;
@@ -209,45 +212,54 @@ __device__ __forceinline__ void peer_store_final(const DecodeArgs &a, int b, int
     }
 }
 
-// After its own units, CTA i merges the pairs p = i, i + gridDim, ... of this call, reading the
-// ranks' words of p's G heads as they arrive:
+// After its own units, every consumer thread of the grid merges a share of this call's
+// (sequence, head, column) elements, reading the ranks' words as they arrive:
 //   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L.
-// A CTA waits only once its own units are done, and no rank's units wait on anything, so the
-// waits cannot form a cycle.  Called by the NW*32 consumer threads.
+// The 3R words of an element are loaded together (one round trip), and only the ones that do
+// not yet carry the call's epoch are read again.  A CTA waits only once its own units are
+// done, and no rank's units wait on anything, so the waits cannot form a cycle.  Called by
+// the NW*32 consumer threads.
 template <int G, int D, int NW>
 __device__ __forceinline__ void peer_merge_pairs(const DecodeArgs &a, int tid) {
     const int R = a.px.nranks;
-    const int pairs = a.nseq * a.nHeadKv;
     const unsigned long long *g = a.px.gather[a.px.rank];
     const int64_t stride = (int64_t)a.nseq * a.nHead * (D + 2);
+    const int64_t total = (int64_t)a.nseq * a.nHead * D;
+    const unsigned epoch = a.px.epoch;
     const uint64_t t0 = globaltimer_ns();
     bool ok = true;
-    for (int p = blockIdx.x; p < pairs && ok; p += gridDim.x) {
-        const int b = p / a.nHeadKv, grp = p - b * a.nHeadKv;
-        for (int e = tid; e < G * D && ok; e += NW * 32) {
-            const int h = e / D, dd = e - h * D;
-            const int64_t row = (int64_t)b * a.nHead + grp * G + h;
-            const unsigned long long *pr = g + row * (D + 2);
-            float m[kMaxPeers], l[kMaxPeers], o[kMaxPeers];
-            float M = -INFINITY;
+    for (int64_t e = (int64_t)blockIdx.x * (NW * 32) + tid; e < total && ok; e += (int64_t)gridDim.x * (NW * 32)) {
+        const int64_t row = e / D;
+        const int dd = (int)(e - row * D);
+        const unsigned long long *pr = g + row * (D + 2);
+        unsigned long long wm[kMaxPeers], wl[kMaxPeers], wo[kMaxPeers];
 #pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r) {
-                if (r >= R) break;
-                m[r] = wait_word(pr + r * stride + D, a.px.epoch, t0, &ok, a.err);
-                l[r] = wait_word(pr + r * stride + D + 1, a.px.epoch, t0, &ok, a.err);
-                o[r] = wait_word(pr + r * stride + dd, a.px.epoch, t0, &ok, a.err);
-                M = fmaxf(M, m[r]);
+        for (int r = 0; r < kMaxPeers; ++r) {
+            if (r < R) {
+                wm[r] = ld_word_sys(pr + r * stride + D);
+                wl[r] = ld_word_sys(pr + r * stride + D + 1);
+                wo[r] = ld_word_sys(pr + r * stride + dd);
             }
-            float L = 0.f, O = 0.f;
-#pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r) {
-                if (r >= R) break;
-                const float w = safe_exp2_diff(m[r], M);
-                L = fmaf(l[r], w, L);
-                O = fmaf(o[r], w, O);
-            }
-            if (ok) a.out[row * D + dd] = (L > 0.f) ? O / L : 0.f;
         }
+        float m[kMaxPeers], l[kMaxPeers], o[kMaxPeers];
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+            if (r >= R) break;
+            m[r] = wait_word(pr + r * stride + D, wm[r], epoch, t0, a.px.wait_ns, &ok, a.err);
+            l[r] = wait_word(pr + r * stride + D + 1, wl[r], epoch, t0, a.px.wait_ns, &ok, a.err);
+            o[r] = wait_word(pr + r * stride + dd, wo[r], epoch, t0, a.px.wait_ns, &ok, a.err);
+            M = fmaxf(M, m[r]);
+        }
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+            if (r >= R) break;
+            const float w = safe_exp2_diff(m[r], M);
+            L = fmaf(l[r], w, L);
+            O = fmaf(o[r], w, O);
+        }
+        if (ok) a.out[row * D + dd] = (L > 0.f) ? O / L : 0.f;
     }
 }
 

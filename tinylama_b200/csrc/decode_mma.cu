@@ -361,6 +361,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
         cu.n = local_len(a, cu.b, err);
         cu.p0 = min(rank * a.chunk, cu.n);
         cu.p1 = min(cu.p0 + a.chunk, cu.n);
+        // the host sized the chunks from its copy of the positions: a longer sequence on the
+        // device would leave positions past the cluster's last chunk unread
+        if (tid == 0 && rank == cl - 1 && (long long)cu.n > (long long)cl * a.chunk) atomicOr(err, TL_DEVERR_BAD_ARG);
     }
 
     if (warp == C::NW) {
@@ -604,7 +607,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     if constexpr (CLU) {
         consume_unit(cu);
         cluster_epilogue<G, D, C::NW>(a, cu, wm, wl, wo, clb, cx, tid, abort_flag);
-        // split-KV across GPUs: CTA i merges pair i (every cluster is resident: the host checks)
+        // split-KV across GPUs: this CTA's share of the cross-rank merge (every cluster is
+        // resident: the host checks)
         if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);
     } else {
         while (true) {
@@ -686,10 +690,10 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
 }
 
 template <typename KV, int D, int G>
-int occ_t() {
+int occ_t(int nseq) {
     using C = MmaCfg<KV, D, G>;
     int n = 0;
-    const size_t smem = C::smem_bytes(256);
+    const size_t smem = C::smem_bytes(nseq);
     auto kern = decode_mma_kernel<KV, D, G, false>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, C::THREADS, smem) != cudaSuccess)
@@ -796,24 +800,44 @@ int decode_mma_cluster_capacity(int headDim, int group, int dtype, int cluster) 
     return n;
 }
 
-int decode_mma_ctas_per_sm(int headDim, int group, int dtype) {
-#define TL_MMA_OCC(KV, DD)                         \
-    switch (group) {                               \
-        case 1: return occ_t<KV, DD, 1>();         \
-        case 2: return occ_t<KV, DD, 2>();         \
-        case 4: return occ_t<KV, DD, 4>();         \
-        case 8: return occ_t<KV, DD, 8>();         \
-        default: return 1;                         \
+int decode_mma_ctas_per_sm(int headDim, int group, int dtype, int nseq) {
+#define TL_MMA_OCC(KV, DD)                             \
+    switch (group) {                                   \
+        case 1: return occ_t<KV, DD, 1>(nseq);         \
+        case 2: return occ_t<KV, DD, 2>(nseq);         \
+        case 4: return occ_t<KV, DD, 4>(nseq);         \
+        case 8: return occ_t<KV, DD, 8>(nseq);         \
+        default: return 1;                             \
     }
     if (dtype == TL_KV_F32) {
-        if (headDim == 64) return group == 8 ? occ_t<float, 64, 8>() : occ_t<float, 64, 4>();
-        if (headDim == 128) return group == 8 ? occ_t<float, 128, 8>() : occ_t<float, 128, 4>();
+        if (headDim == 64) return group == 8 ? occ_t<float, 64, 8>(nseq) : occ_t<float, 64, 4>(nseq);
+        if (headDim == 128) return group == 8 ? occ_t<float, 128, 8>(nseq) : occ_t<float, 128, 4>(nseq);
     } else {
         if (headDim == 64) { TL_MMA_OCC(__nv_bfloat16, 64) }
         if (headDim == 128) { TL_MMA_OCC(__nv_bfloat16, 128) }
     }
 #undef TL_MMA_OCC
     return 1;
+}
+
+size_t decode_mma_smem_bytes(int headDim, int group, int dtype, int nseq) {
+#define TL_MMA_SMEM(KV, DD)                                              \
+    switch (group) {                                                     \
+        case 1: return MmaCfg<KV, DD, 1>::smem_bytes(nseq);              \
+        case 2: return MmaCfg<KV, DD, 2>::smem_bytes(nseq);              \
+        case 4: return MmaCfg<KV, DD, 4>::smem_bytes(nseq);              \
+        case 8: return MmaCfg<KV, DD, 8>::smem_bytes(nseq);              \
+        default: return 0;                                               \
+    }
+    if (dtype == TL_KV_F32) {
+        if (headDim == 64) { TL_MMA_SMEM(float, 64) }
+        if (headDim == 128) { TL_MMA_SMEM(float, 128) }
+    } else {
+        if (headDim == 64) { TL_MMA_SMEM(__nv_bfloat16, 64) }
+        if (headDim == 128) { TL_MMA_SMEM(__nv_bfloat16, 128) }
+    }
+#undef TL_MMA_SMEM
+    return 0;
 }
 
 }  // namespace tl

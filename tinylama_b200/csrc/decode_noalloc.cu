@@ -12,7 +12,13 @@
 //
 // Limits: the array holds kNoAllocBytes = 16 MiB.  At most kNoAllocCounters = 65536
 // (sequence, kv-head) pairs per call; the chunk length is raised until the partials fit in
-// what remains, and a call that cannot fit is refused with TL_ERR_INVALID.
+// what remains, and a call that cannot fit is refused with TL_ERR_INVALID.  The decode kernel
+// keeps two ints per sequence in shared memory, so the number of sequences is also bounded by
+// the device's shared memory per block (checked before the launch, TL_ERR_INVALID).
+//
+// With no handle there is no tl_check_device: when the kernel refuses a call on the device
+// (positions on the device that disagree with pos_host, a position past maxLen, a timed-out
+// wait), a second small kernel fills `out` with NaN, so that the caller can see it.
 //
 // The first call on a device looks the array's device address up with cudaGetSymbolAddress
 // (with that device current); make that first call before any stream capture.  Every call
@@ -52,6 +58,14 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 std::mutex g_mu;
 void *g_scratch_dev[kMaxDevices] = {};
+
+// After the decode kernel: if it recorded an error, every output element becomes NaN.
+__global__ void poison_on_error_kernel(const unsigned *err, float *out, size_t n) {
+    if (*reinterpret_cast<const volatile unsigned *>(err) == 0u) return;
+    const float nan = __int_as_float(0x7fc00000);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = nan;
+}
 
 int scratch_for_current_device(void **out) {
     int dev = -1;
@@ -103,11 +117,21 @@ extern "C" int tl_decode_attention_noalloc(const float *q, const void *k_cache, 
     void *scratch = nullptr;
     int rc = scratch_for_current_device(&scratch);
     if (rc != TL_OK) return rc;
-    int dev = 0, sms = 0;
+    int dev = 0, sms = 0, smem_max = 0;
     cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-        return api_fail(TL_ERR_CUDA, "cudaDeviceGetAttribute(multiProcessorCount) failed");
-    const int ctas = sms * decode_ctas_per_sm(headDim, G, kvDtype);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0 ||
+        cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        return api_fail(TL_ERR_CUDA, "cudaDeviceGetAttribute failed");
+    const size_t smem = decode_smem_bytes(headDim, G, kvDtype, nseq);
+    if (smem > (size_t)smem_max) {
+        char m[200];
+        snprintf(m, sizeof m,
+                 "nseq %d needs %zu bytes of shared memory in the decode kernel, more than the %d per block "
+                 "of this device: split the batch",
+                 nseq, smem, smem_max);
+        return api_fail(TL_ERR_INVALID, m);
+    }
+    const int ctas = sms * decode_ctas_per_sm(headDim, G, kvDtype, nseq);
 
     // chunk length: the usual balance target, raised until the partials fit the scratch
     long long want = (tot * nHeadKv + (long long)ctas * 4 - 1) / ((long long)ctas * 4);
@@ -167,6 +191,11 @@ extern "C" int tl_decode_attention_noalloc(const float *q, const void *k_cache, 
     a.lse_out = nullptr;
     e = launch_decode(a, (int)std::max<long long>(1, std::min<long long>(units, ctas)), s);
     if (e == cudaErrorNotSupported) return api_fail(TL_ERR_UNSUPPORTED, "decode: shape not covered");
+    if (e != cudaSuccess) return api_fail(TL_ERR_CUDA, cudaGetErrorString(e));
+    const size_t n_out = (size_t)nseq * nHead * headDim;
+    const int blocks = (int)std::min<size_t>((n_out + 1023) / 1024, (size_t)sms * 4);
+    poison_on_error_kernel<<<blocks, 256, 0, s>>>(a.err, out, n_out);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return api_fail(TL_ERR_CUDA, cudaGetErrorString(e));
     return TL_OK;
 }

@@ -28,8 +28,12 @@
 
 #include <stdlib.h>
 
+#include <sched.h>
+
 #include <algorithm>
+#include <chrono>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "internal.h"
@@ -57,7 +61,12 @@ struct Nccl {
     ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*CommDestroy)(ncclComm_t);
     const char *(*GetErrorString)(ncclResult_t);
-    bool ok;
+    // non-blocking set-up (NCCL >= 2.14): an init that a rank never joins can be given up
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *);
+    ncclResult_t (*CommAbort)(ncclComm_t);
+    ncclResult_t (*CommFinalize)(ncclComm_t);
+    bool ok, nonblocking;
 };
 
 const Nccl &nccl() {
@@ -73,7 +82,12 @@ const Nccl &nccl() {
         n.AllGather = reinterpret_cast<decltype(n.AllGather)>(dlsym(h, "ncclAllGather"));
         n.CommDestroy = reinterpret_cast<decltype(n.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
         n.GetErrorString = reinterpret_cast<decltype(n.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+        n.CommInitRankConfig = reinterpret_cast<decltype(n.CommInitRankConfig)>(dlsym(h, "ncclCommInitRankConfig"));
+        n.CommGetAsyncError = reinterpret_cast<decltype(n.CommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
+        n.CommAbort = reinterpret_cast<decltype(n.CommAbort)>(dlsym(h, "ncclCommAbort"));
+        n.CommFinalize = reinterpret_cast<decltype(n.CommFinalize)>(dlsym(h, "ncclCommFinalize"));
         n.ok = n.GetUniqueId && n.CommInitRank && n.AllGather && n.CommDestroy && n.GetErrorString;
+        n.nonblocking = n.CommInitRankConfig && n.CommGetAsyncError && n.CommAbort && n.CommFinalize;
     });
     return n;
 }
@@ -82,6 +96,26 @@ int nccl_fail(ncclResult_t r, const char *what) {
     char buf[256];
     snprintf(buf, sizeof buf, "%s: %s", what, nccl().ok ? nccl().GetErrorString(r) : "NCCL unavailable");
     return api_fail(TL_ERR_NCCL, buf);
+}
+
+long long env_ms(const char *name, long long dflt) {
+    const char *e = getenv(name);
+    if (!e || !*e) return dflt;
+    const long long v = atoll(e);
+    return v > 0 ? v : dflt;
+}
+
+// On a non-blocking communicator an NCCL call may return before its work is enqueued: poll
+// until it is, or until the operation fails.  A blocking communicator returns at once.
+ncclResult_t nccl_settle(const tl_attn *h, ncclResult_t r) {
+    if (!nccl().nonblocking || (r != ncclSuccess && r != ncclInProgress)) return r;
+    const auto comm = reinterpret_cast<ncclComm_t>(h->comm);
+    ncclResult_t st = ncclInProgress;
+    while (true) {
+        if (nccl().CommGetAsyncError(comm, &st) != ncclSuccess) return ncclInternalError;
+        if (st != ncclInProgress) return st;
+        sched_yield();
+    }
 }
 
 #define TL_NEED_NCCL()                                                                   \
@@ -93,7 +127,8 @@ int nccl_fail(ncclResult_t r, const char *what) {
 int dist_barrier(tl_attn *h) {
     float *d = nullptr;
     if (cudaMalloc(&d, sizeof(float) * h->nranks) != cudaSuccess) return api_fail(TL_ERR_NOMEM, "barrier buffer");
-    ncclResult_t r = nccl().AllGather(d + h->rank, d, 1, ncclFloat, reinterpret_cast<ncclComm_t>(h->comm), h->stream);
+    ncclResult_t r = nccl_settle(
+        h, nccl().AllGather(d + h->rank, d, 1, ncclFloat, reinterpret_cast<ncclComm_t>(h->comm), h->stream));
     cudaStreamSynchronize(h->stream);
     cudaFree(d);
     return r == ncclSuccess ? TL_OK : nccl_fail(r, "ncclAllGather (barrier)");
@@ -109,16 +144,23 @@ void unmap_peers(tl_attn *h) {
 // Collective: export this rank's exchange buffer, all-gather the IPC handles, map the peers'.
 // Returns TL_OK with peerBase[rank] == nullptr when the peers cannot be mapped (the NCCL
 // exchange is used then).
-int map_peers(tl_attn *h) {
+int map_peers(tl_attn *h, bool silent_peer) {
     const char *env = getenv("TL_DIST_NCCL");
     const bool want = h->nranks <= kMaxPeers && !(env && env[0] == '1');
-    const size_t half = (size_t)h->nranks * h->maxBatch * h->nHead * (h->headDim + 2);
+    const int slots = h->nranks + (silent_peer ? 1 : 0);
+    const size_t half = (size_t)slots * h->maxBatch * h->nHead * (h->headDim + 2);
     const size_t bytes = 2 * half * sizeof(unsigned long long);
     if (want) {
         if (cudaMalloc(&h->dPeerBuf, bytes) != cudaSuccess)
             return api_fail(TL_ERR_NOMEM, "split-KV exchange buffer allocation failed");
         cudaMemset(h->dPeerBuf, 0, bytes);  // every word starts at epoch 0
         h->peerHalfWords = half;
+        if (silent_peer) {
+            // the injected rank's buffer: this rank stores into it, nothing ever writes ours
+            if (cudaMalloc(&h->dSilentPeer, bytes) != cudaSuccess)
+                return api_fail(TL_ERR_NOMEM, "split-KV exchange buffer allocation failed");
+            cudaMemset(h->dSilentPeer, 0, bytes);
+        }
     }
     // every rank takes part in the handle exchange, also one that does not map (all-or-nothing)
     cudaIpcMemHandle_t mine{};
@@ -132,8 +174,8 @@ int map_peers(tl_attn *h) {
     memcpy(me.data() + sizeof mine, &ok, sizeof ok);
     cudaMemcpy(dev + rec * h->rank, me.data(), rec, cudaMemcpyHostToDevice);
     cudaDeviceSynchronize();  // the zeroed words are in place before any peer can map them
-    ncclResult_t r = nccl().AllGather(dev + rec * h->rank, dev, rec, ncclChar, reinterpret_cast<ncclComm_t>(h->comm),
-                                      h->stream);
+    ncclResult_t r = nccl_settle(h, nccl().AllGather(dev + rec * h->rank, dev, rec, ncclChar,
+                                                     reinterpret_cast<ncclComm_t>(h->comm), h->stream));
     cudaStreamSynchronize(h->stream);
     cudaMemcpy(host.data(), dev, rec * h->nranks, cudaMemcpyDeviceToHost);
     cudaFree(dev);
@@ -164,7 +206,8 @@ int map_peers(tl_attn *h) {
         char *d2 = nullptr;
         if (cudaMalloc(&d2, rec * h->nranks) != cudaSuccess) return api_fail(TL_ERR_NOMEM, "handle exchange buffer");
         cudaMemcpy(d2 + rec * h->rank, again.data(), rec, cudaMemcpyHostToDevice);
-        r = nccl().AllGather(d2 + rec * h->rank, d2, rec, ncclChar, reinterpret_cast<ncclComm_t>(h->comm), h->stream);
+        r = nccl_settle(h, nccl().AllGather(d2 + rec * h->rank, d2, rec, ncclChar,
+                                            reinterpret_cast<ncclComm_t>(h->comm), h->stream));
         cudaStreamSynchronize(h->stream);
         cudaMemcpy(host.data(), d2, rec * h->nranks, cudaMemcpyDeviceToHost);
         cudaFree(d2);
@@ -197,22 +240,97 @@ int tl_dist_unique_id(char *id128) {
 int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank) {
     if (!h || !id128) return api_fail(TL_ERR_INVALID, "NULL argument");
     if (nranks < 1 || rank < 0 || rank >= nranks) return api_fail(TL_ERR_INVALID, "bad rank/nranks");
+    if (nranks > kMaxPeers) return api_fail(TL_ERR_INVALID, "at most 8 ranks (one NVSwitch domain)");
     if (h->comm) return api_fail(TL_ERR_INVALID, "handle already joined a communicator");
     TL_NEED_NCCL();
+    const char *fault = getenv("TL_DIST_FAULT_SILENT_PEER");
+    const bool silent = fault && fault[0] == '1';
+    if (silent && nranks != 1)
+        return api_fail(TL_ERR_INVALID, "TL_DIST_FAULT_SILENT_PEER injects a peer into a one-rank group only");
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(h->device);
     ncclUniqueId id;
     memcpy(&id, id128, sizeof id);
-    ncclComm_t comm;
-    ncclResult_t r = nccl().CommInitRank(&comm, nranks, id, rank);
+    ncclComm_t comm = nullptr;
+    ncclResult_t r;
+    if (nccl().nonblocking) {
+        // non-blocking set-up, given up after TL_DIST_INIT_TIMEOUT_MS (default 120 s) if some
+        // rank never joins: the call then fails instead of waiting for ever
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        const long long limit_ms = env_ms("TL_DIST_INIT_TIMEOUT_MS", 120000);
+        r = nccl().CommInitRankConfig(&comm, nranks, id, rank, &cfg);
+        if (r == ncclSuccess || r == ncclInProgress) {
+            const auto t0 = std::chrono::steady_clock::now();
+            ncclResult_t st = ncclInProgress;
+            while (true) {
+                if (nccl().CommGetAsyncError(comm, &st) != ncclSuccess) st = ncclInternalError;
+                if (st != ncclInProgress) break;
+                const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                                    std::chrono::steady_clock::now() - t0).count();
+                if (ms > limit_ms) break;
+                std::this_thread::sleep_for(std::chrono::milliseconds(1));
+            }
+            if (st == ncclInProgress) {
+                nccl().CommAbort(comm);
+                cudaSetDevice(prev);
+                char m[192];
+                snprintf(m, sizeof m, "tl_dist_init: the group of %d ranks did not form within %lld ms (a rank "
+                         "never joined); the communicator was aborted", nranks, limit_ms);
+                return api_fail(TL_ERR_NCCL, m);
+            }
+            r = st;
+            if (r != ncclSuccess) nccl().CommAbort(comm);
+        }
+    } else {
+        r = nccl().CommInitRank(&comm, nranks, id, rank);
+    }
     cudaSetDevice(prev);
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
     h->comm = comm;
     h->nranks = nranks;
     h->rank = rank;
+    h->epoch = 0;
+    h->peerWaitNs = (unsigned long long)env_ms("TL_DIST_WAIT_MS", 2000) * 1000000ull;
     cudaSetDevice(h->device);
-    const int rc = map_peers(h);
+    const int rc = map_peers(h, silent);
+    cudaSetDevice(prev);
+    return rc;
+}
+
+int tl_dist_resync(tl_attn *h) {
+    if (!h) return api_fail(TL_ERR_INVALID, "NULL handle");
+    if (!h->comm) return api_fail(TL_ERR_INVALID, "tl_dist_init has not been called");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(h->device);
+    // this rank's calls have ended (completed or given up): no kernel of it still writes words
+    cudaError_t e = cudaDeviceSynchronize();
+    int rc = TL_OK;
+    unsigned *d = nullptr;
+    if (e != cudaSuccess) {
+        rc = api_fail(TL_ERR_CUDA, cudaGetErrorString(e));
+    } else if (cudaMalloc(&d, sizeof(unsigned) * h->nranks) != cudaSuccess) {
+        rc = api_fail(TL_ERR_NOMEM, "resync buffer");
+    } else {
+        std::vector<unsigned> all(h->nranks);
+        cudaMemcpy(d + h->rank, &h->epoch, sizeof(unsigned), cudaMemcpyHostToDevice);
+        ncclResult_t r = nccl_settle(h, nccl().AllGather(d + h->rank, d, 1, ncclUint32,
+                                                         reinterpret_cast<ncclComm_t>(h->comm), h->stream));
+        cudaStreamSynchronize(h->stream);
+        if (r != ncclSuccess) {
+            rc = nccl_fail(r, "ncclAllGather (resync)");
+        } else {
+            cudaMemcpy(all.data(), d, sizeof(unsigned) * h->nranks, cudaMemcpyDeviceToHost);
+            // every word any rank has stored carries an epoch <= the largest one used so far:
+            // the next call, at a larger epoch, reads none of them
+            unsigned mx = 0;
+            for (unsigned x : all) mx = std::max(mx, x);
+            h->epoch = mx;
+        }
+        cudaFree(d);
+    }
     cudaSetDevice(prev);
     return rc;
 }
@@ -234,6 +352,11 @@ void tl_dist_finalize(tl_attn *h) {
         h->peerHalfWords = 0;
         h->epoch = 0;
     }
+    if (h->dSilentPeer) {
+        cudaFree(h->dSilentPeer);
+        h->dSilentPeer = nullptr;
+    }
+    if (nccl().nonblocking) nccl_settle(h, nccl().CommFinalize(reinterpret_cast<ncclComm_t>(h->comm)));
     nccl().CommDestroy(reinterpret_cast<ncclComm_t>(h->comm));
     cudaSetDevice(prev);
     h->comm = nullptr;
@@ -262,6 +385,12 @@ int tl_decode_attention_dist(tl_attn *h, int layer, int slot0, int nseq, const i
         for (int r = 0; r < h->nranks; ++r) px.gather[r] = reinterpret_cast<unsigned long long *>(h->peerBase[r]) + half;
         px.nranks = h->nranks;
         px.rank = h->rank;
+        px.wait_ns = h->peerWaitNs;
+        if (h->dSilentPeer) {
+            // injected fault: a second rank whose words never arrive
+            px.gather[1] = reinterpret_cast<unsigned long long *>(h->dSilentPeer) + half;
+            px.nranks = 2;
+        }
         const int rc = api_run_decode_peer(h, layer, slot0, nseq, pos_dev, pos_host, q, out, s,
                                            h->rank * h->maxLen, px);
         cudaSetDevice(prev);
@@ -286,8 +415,8 @@ int tl_decode_attention_dist(tl_attn *h, int layer, int slot0, int nseq, const i
     rc = api_run_decode_lse(h, layer, slot0, nseq, pos_dev, pos_host, q, mine, s,
                             h->rank * h->maxLen);
     if (rc == TL_OK) {
-        ncclResult_t r = nccl().AllGather(mine, h->dGather, per_rank, ncclFloat,
-                                       reinterpret_cast<ncclComm_t>(h->comm), s);
+        ncclResult_t r = nccl_settle(h, nccl().AllGather(mine, h->dGather, per_rank, ncclFloat,
+                                                         reinterpret_cast<ncclComm_t>(h->comm), s));
         if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather");
     }
     if (rc == TL_OK) {

@@ -90,6 +90,10 @@ struct tl_attn {
     void *peerBase[tl::kMaxPeers] = {};
     size_t peerHalfWords = 0;
     unsigned epoch = 0;
+    unsigned long long peerWaitNs = 2000000000ull;  // TL_DIST_WAIT_MS at tl_dist_init
+    // host-side fault injection (TL_DIST_FAULT_SILENT_PEER=1 at tl_dist_init, one rank only):
+    // the exchange runs as rank 0 of two, and rank 1 is a local buffer that nothing writes
+    void *dSilentPeer = nullptr;
 };
 
 namespace tl {
@@ -188,14 +192,19 @@ struct DecodeArgs {
         unsigned long long *gather[kMaxPeers];  // rank r's half for this call: [nranks][nseq*nHead][D+2]
         unsigned epoch;
         int nranks, rank;
+        unsigned long long wait_ns;             // limit of each wait for a peer's words
     } px;
 };
 cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s);
-int decode_ctas_per_sm(int headDim, int group, int dtype);
+// Resident CTAs per SM of the decode kernel a launch for nseq sequences uses.
+int decode_ctas_per_sm(int headDim, int group, int dtype, int nseq);
+// Dynamic shared memory of that launch (bytes).
+size_t decode_smem_bytes(int headDim, int group, int dtype, int nseq);
 // tensor-core decode for bf16 caches (decode_mma.cu)
 bool decode_mma_covers(int headDim, int group, int dtype);
 cudaError_t launch_decode_mma(const DecodeArgs &a, int num_ctas, cudaStream_t s);
-int decode_mma_ctas_per_sm(int headDim, int group, int dtype);
+int decode_mma_ctas_per_sm(int headDim, int group, int dtype, int nseq);
+size_t decode_mma_smem_bytes(int headDim, int group, int dtype, int nseq);
 // Clusters of `cluster` CTAs of the tensor-core decode kernel that can be resident at once
 // (cudaOccupancyMaxActiveClusters; 0 if the query fails).
 int decode_mma_cluster_capacity(int headDim, int group, int dtype, int cluster);

@@ -184,7 +184,7 @@ bool plan_cluster(const tl_attn *h, int nseq, int nmax, long long tot, int ctas,
 Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset, int slice,
                  bool cluster_ok = false, bool exchange = false) {
     const int G = h->nHead / h->nHeadKv;
-    const int occ = decode_ctas_per_sm(h->headDim, G, h->kvDtype);
+    const int occ = decode_ctas_per_sm(h->headDim, G, h->kvDtype, nseq);
     const int ctas = h->numSms * occ;
     long long tot = 0;
     int nmax = 0;
