@@ -406,6 +406,7 @@ def north_star_subs(args, dist) -> dict:
             out[f"prefill_{k}_step_frac"] = d["frac_of_bf16_peak"]
     sk = run_splitkv(args, dist, L=args.ctx_len)
     out["splitkv_131072_us"] = round(sk["ms_per_step"] * 1e3, 1)
+    out["splitkv_131072_local_shard_us"] = round(sk["local_shard_ms"] * 1e3, 1)
     out["splitkv_131072_frac_per_gpu"] = sk["roofline"]["frac"]
     tiny = run_decode_tiny(args, dist)
     for L, d in tiny["by_ctx_len"].items():
@@ -736,6 +737,18 @@ def run_splitkv(args, dist, B=4, Hq=32, Hkv=8, D=128, L=131072, base=500000.0):
 
         ms = time_steps(step, args.steps, args.warmup, stream, dist)
         _lib.check(_lib.lib.tl_check_device(h, sp))
+        # the same shard attended alone (no exchange, no merge across ranks): what the step
+        # costs beyond it is the exchange and the ranks' skew
+        shard_pos = np.full(B, slice_len - 1, np.int32)
+        dshard = torch.from_numpy(shard_pos).cuda()
+        local_out = torch.empty_like(out)
+
+        def local():
+            _lib.check(_lib.lib.tl_decode_attention(h, 0, 0, B, p(dshard), shard_pos.ctypes.data_as(C.c_void_p),
+                                                    p(q), p(local_out), sp))
+
+        ms_local = time_steps(local, args.steps, args.warmup, stream, dist)
+        _lib.check(_lib.lib.tl_check_device(h, sp))
         kv_bytes = B * L * Hkv * D * 2 * 2
         pk = peaks()
         gbs = kv_bytes / (ms / 1e3) / 1e9
@@ -749,6 +762,7 @@ def run_splitkv(args, dist, B=4, Hq=32, Hkv=8, D=128, L=131072, base=500000.0):
                        "rope_theta": base, "kv_dtype": "bf16", "parallelism": f"split-KV x{n}, fused peer-memory exchange and merge" if os.environ.get("TL_DIST_NCCL") != "1" else f"split-KV x{n} + NCCL all-gather merge",
                        "l2": f"no flush: {kv_bytes / n / 1e9:.2f} GB of KV per GPU per step > 126 MB L2"},
             "hbm_gbs_aggregate": round(gbs, 1), "hbm_gbs_per_gpu": round(gbs / n, 1),
+            "local_shard_ms": round(ms_local, 4),
             "roofline": {"bound": "hbm", "achieved": round(gbs / n, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / n / pk["hbm_gbs"], 4), "peak_src": pk["src"],
                          "note": "per GPU, whole step (local attention, exchange and merge)"},

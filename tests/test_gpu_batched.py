@@ -351,3 +351,69 @@ def test_decode_cluster_mode_matches_queue_mode(env, kvd, Hq, Hkv, D, lens):
         os.environ.pop("TL_DECODE_CLUSTER", None)
         if old is not None:
             os.environ["TL_DECODE_CLUSTER"] = old
+
+
+@pytest.mark.parametrize("kvd,Hq,Hkv,D,ropeDim,lens", [
+    (0, 32, 4, 64, 64, [128]),               # TinyLlama batch 1 (f32 cache, tf32 tensor-core path)
+    (0, 32, 4, 64, 64, [2048]),
+    (0, 32, 4, 64, 32, [64, 257]),           # partial rotary; new rows at tile boundaries
+    (1, 32, 8, 128, 128, [100, 700, 1]),     # bf16 cache, head_dim 128, a one-position sequence
+    (1, 8, 8, 64, 64, [255, 256]),           # G = 1
+])
+def test_decode_step_fused_equals_two_launches(env, kvd, Hq, Hkv, D, ropeDim, lens):
+    """In cluster mode tl_decode_step runs as one launch: the decode kernel rotates q and the new
+    k at the step's position and writes k and v into the cache itself.  TL_DECODE_FUSE=0 runs
+    the RoPE/append kernel first, as before.  Both must give the same bits: the output, q and k
+    rotated in place, and the cache (the new row and everything else)."""
+    torch, _lib = env
+    rng = np.random.default_rng(sum(lens) + D + ropeDim)
+    base = 10000.0
+    B = len(lens)
+    maxLen = max(lens) + 3
+    pos = np.array(lens, np.int32)  # the new token sits at position L
+    q, k, v = randn(rng, B, Hq * D), randn(rng, B, Hkv * D), randn(rng, B, Hkv * D)
+    kc0, vc0 = randn(rng, B, maxLen, Hkv * D), randn(rng, B, maxLen, Hkv * D)
+    results = []
+    old = os.environ.pop("TL_DECODE_FUSE", None)
+    try:
+        for mode in ("1", "0"):
+            os.environ["TL_DECODE_FUSE"] = mode
+            h = C.c_void_p()
+            _lib.check(_lib.lib.tl_attn_create(C.byref(h), 1, Hq, Hkv, D, ropeDim, base, maxLen, B, kvd, 0))
+            try:
+                for b in range(B):
+                    kk, vv = torch.from_numpy(kc0[b]).cuda(), torch.from_numpy(vc0[b]).cuda()
+                    _lib.check(_lib.lib.tl_kv_store(h, 0, b, 0, ptr(kk), ptr(vv), maxLen, None))
+                dq, dk, dv = (torch.from_numpy(a.copy()).cuda() for a in (q, k, v))
+                dpos = torch.from_numpy(pos).cuda()
+                out = torch.empty(B, Hq * D, device="cuda")
+                _lib.check(_lib.lib.tl_decode_step(h, 0, 0, B, ptr(dpos), pos.ctypes.data_as(C.c_void_p),
+                                                   ptr(dq), ptr(dk), ptr(dv), ptr(out), None))
+                _lib.check(_lib.lib.tl_check_device(h, None))
+                caches = []
+                for b in range(B):
+                    kr = np.empty((Hkv * D, maxLen), np.float32)
+                    vr = np.empty((Hkv * D, maxLen), np.float32)
+                    _lib.check(_lib.lib.tl_kv_read(h, 0, b, kr.ctypes.data_as(C.c_void_p), vr.ctypes.data_as(C.c_void_p)))
+                    caches.append((kr, vr))
+                results.append((out.cpu().numpy(), dq.cpu().numpy(), dk.cpu().numpy(), caches))
+            finally:
+                _lib.lib.tl_attn_destroy(h)
+    finally:
+        os.environ.pop("TL_DECODE_FUSE", None)
+        if old is not None:
+            os.environ["TL_DECODE_FUSE"] = old
+    (o1, q1, k1, c1), (o0, q0, k0, c0) = results
+    assert np.array_equal(q1, q0) and np.array_equal(k1, k0)
+    for b in range(B):
+        assert np.array_equal(c1[b][0], c0[b][0]) and np.array_equal(c1[b][1], c0[b][1]), b
+    assert np.array_equal(o1, o0), float(np.max(np.abs(o1 - o0)))
+    # and the rotation is the reference's (applyRopeAtPos, src/forward.nim:125-139): within 2
+    # ulps of the row's magnitude.  At one position a pair whose cos/sin differ from glibc's in
+    # the last bit moves that pair in every head, so the bit-identical share is lower than over
+    # many positions (1 pair in 32 is 3 %).
+    from tests.helpers import rope_agrees
+    for b, L in enumerate(lens):
+        for got, x, H in ((q1[b], q[b], Hq), (k1[b], k[b], Hkv)):
+            same, ulps = rope_agrees(got.reshape(-1, 1), ora.rope_at_pos(x.reshape(-1, 1), H, D, ropeDim, base, L))
+            assert ulps <= 2 and same >= 0.9, (b, L, same, ulps)

@@ -155,6 +155,24 @@ __device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
     return r != 0;
 }
 
+// ---- RoPE --------------------------------------------------------------------------------
+// Pair rotation (x0, x1) -> (x0*c - x1*s, x0*s + x1*c) with explicit round-to-nearest
+// multiplies and adds (no contraction into multiply-adds), as the reference evaluates it in
+// float32 (src/forward.nim:119-123).
+__device__ __forceinline__ void rope_rotate(float x0, float x1, float c, float s, float &y0, float &y1) {
+    y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+// cos/sin of the float32 angle float32(pos) * theta: evaluated in double and rounded to float32
+// (the correctly rounded values a libm's cosf/sinf return).
+__device__ __forceinline__ float2 rope_cos_sin(int pos, float theta) {
+    const float angle = __fmul_rn((float)pos, theta);
+    double sd, cd;
+    sincos((double)angle, &sd, &cd);
+    return make_float2((float)cd, (float)sd);
+}
+
 // ---- element conversion ------------------------------------------------------------------
 template <typename T> struct KvT;
 template <> struct KvT<float> {

@@ -223,10 +223,25 @@ __device__ __forceinline__ void cluster_final(const DecodeArgs &a, int b, int he
 //   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L
 // into out, and releases each of them (their shared memory must stay until it has read it).
 // Every wait is bounded, and every CTA arrives whatever its own state, so none waits for ever.
+// Fused decode step: the rotated q of the cluster's G heads written back into the input, by
+// rank 0 once every CTA of the cluster has read q (the tl_decode_step contract rotates q in place).
+template <int G, int D, int NW>
+__device__ __forceinline__ void fuse_write_q(const DecodeArgs &a, const Unit &un, const float2 *cs, int tid) {
+    for (int e = 2 * tid; e < G * D; e += 2 * NW * 32) {
+        const int h = e / D, dd = e - h * D, i = dd >> 1;
+        if (i >= a.fz.tab.pairs) continue;
+        const int64_t idx = ((int64_t)un.b * a.nHead + un.g * G + h) * D + dd;
+        float x0 = a.fz.q[idx], x1 = a.fz.q[idx + 1];
+        rope_rotate(x0, x1, cs[i].x, cs[i].y, x0, x1);
+        a.fz.q[idx] = x0;
+        a.fz.q[idx + 1] = x1;
+    }
+}
+
 template <int G, int D, int NW>
 __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit &un, const float *wm, const float *wl,
                                                  const float *wo, uint64_t *clb, float *cx, int tid,
-                                                 volatile int *abort_flag) {
+                                                 volatile int *abort_flag, const float2 *fz_cs) {
     named_bar(1, NW * 32);
     float *cm = cx, *cl = cx + G, *co = cx + 2 * G;
     for (int e = tid; e < G * D; e += NW * 32) {
@@ -252,6 +267,7 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
             const int h = e / D, dd = e - h * D;
             cluster_final<D>(a, un.b, un.g * G + h, dd, co[e], cm[h], cl[h]);
         }
+        if (a.fz.k != nullptr) fuse_write_q<G, D, NW>(a, un, fz_cs, tid);
         return;
     }
     if (rank != 0) {
@@ -261,6 +277,8 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
         return;
     }
     const bool ok = __all_sync(0xffffffffu, mbar_wait_cluster(&clb[0], 0, a.err, abort_flag));
+    // every CTA of the cluster has arrived, so every one has read q
+    if (ok && a.fz.k != nullptr) fuse_write_q<G, D, NW>(a, un, fz_cs, tid);
     if (ok) {
         for (int e = tid; e < G * D; e += NW * 32) {
             const int h = e / D, dd = e - h * D;
@@ -365,6 +383,16 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
         // device would leave positions past the cluster's last chunk unread
         if (tid == 0 && rank == cl - 1 && (long long)cu.n > (long long)cl * a.chunk) atomicOr(err, TL_DEVERR_BAD_ARG);
     }
+    // a decode step fused into this launch (cluster mode): the cos/sin of this sequence's
+    // position, for the rotation of q (every CTA) and of the new k (the CTA whose chunk holds it)
+    __shared__ float2 fz_cs[64];
+    const bool fuse = CLU && a.fz.k != nullptr;
+    const int fz_pos = fuse ? a.pos[cu.b] : -1;
+    if (fuse && warp < C::NW) {
+        for (int i = tid; i < D / 2; i += C::NW * 32)
+            fz_cs[i] = i < a.fz.tab.pairs ? rope_cos_sin(fz_pos, a.fz.tab.theta[i]) : make_float2(1.f, 0.f);
+        named_bar(1, C::NW * 32);
+    }
 
     if (warp == C::NW) {
         // ================= producer =================
@@ -436,6 +464,11 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                 if constexpr (C::F32) {
                     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (row_ok) x = *reinterpret_cast<const float4 *>(qrow + 32 * (kt >> 1) + 4 * (2 * tq + (kt & 1)));
+                    if (fuse) {  // columns c, c+1 and c+2, c+3: pairs c/2 and c/2 + 1
+                        const int pr0 = 16 * (kt >> 1) + 2 * (2 * tq + (kt & 1));
+                        if (pr0 < a.fz.tab.pairs) rope_rotate(x.x, x.y, fz_cs[pr0].x, fz_cs[pr0].y, x.x, x.y);
+                        if (pr0 + 1 < a.fz.tab.pairs) rope_rotate(x.z, x.w, fz_cs[pr0 + 1].x, fz_cs[pr0 + 1].y, x.z, x.w);
+                    }
                     split_tf32(x.x, qh[kt][0], ql[kt][0]);
                     split_tf32(x.y, qh[kt][1], ql[kt][1]);
                     split_tf32(x.z, qh[kt][2], ql[kt][2]);
@@ -446,6 +479,11 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                         const float2 lo = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq);
                         const float2 hi = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq + 8);
                         x0 = lo.x; x1 = lo.y; x2 = hi.x; x3 = hi.y;
+                    }
+                    if (fuse) {  // columns 16kt + 2tq (+1) and 16kt + 8 + 2tq (+1)
+                        const int pr0 = 8 * kt + tq, pr1 = 8 * kt + 4 + tq;
+                        if (pr0 < a.fz.tab.pairs) rope_rotate(x0, x1, fz_cs[pr0].x, fz_cs[pr0].y, x0, x1);
+                        if (pr1 < a.fz.tab.pairs) rope_rotate(x2, x3, fz_cs[pr1].x, fz_cs[pr1].y, x2, x3);
                     }
                     split2(x0, x1, qh[kt][0], ql[kt][0]);
                     split2(x2, x3, qh[kt][1], ql[kt][1]);
@@ -463,6 +501,44 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             const uint32_t kbox = smem_u32(smem + C::OFF_STAGES + stage * C::STAGE_BYTES);
             const uint32_t vbox = kbox + C::TILE_BYTES;
             const int r0 = warp * 16;  // first tile row of this warp
+            if (fuse) {
+                // the new token's row: the tile was loaded before the step's k and v were in the
+                // cache, so the warp that owns the row writes it -- rotated k, and v -- into the
+                // tile, into the cache and (k) back into its input
+                const int rr = fz_pos - p;
+                if (rr >= r0 && rr < r0 + 16 && fz_pos < un.p1) {
+                    for (int i = lane; i < D / 2; i += 32) {
+                        const int64_t src = ((int64_t)un.b * a.nHeadKv + un.g) * D + 2 * i;
+                        float k0 = a.fz.k[src], k1 = a.fz.k[src + 1];
+                        if (i < a.fz.tab.pairs) {
+                            rope_rotate(k0, k1, fz_cs[i].x, fz_cs[i].y, k0, k1);
+                            a.fz.k[src] = k0;
+                            a.fz.k[src + 1] = k1;
+                        }
+                        const float v0 = a.fz.v[src], v1 = a.fz.v[src + 1];
+                        const int64_t dst = a.kv.row(a.layer, a.slot0 + un.b, un.g, fz_pos) * D + 2 * i;
+                        const int col = (2 * i) % C::BOX_COLS;
+                        const uint32_t off = (uint32_t)((2 * i) / C::BOX_COLS) * C::HALF_BYTES;
+                        const uint32_t byte = (uint32_t)(col * (int)sizeof(KV)) & 15u;
+                        const int chunk = col * (int)sizeof(KV) / 16;
+                        uint8_t *ks = smem_raw + (swz(kbox + off, rr, chunk) - raw) + byte;
+                        uint8_t *vs = smem_raw + (swz(vbox + off, rr, chunk) - raw) + byte;
+                        if constexpr (C::F32) {
+                            *reinterpret_cast<float2 *>(reinterpret_cast<float *>(a.kv.k) + dst) = make_float2(k0, k1);
+                            *reinterpret_cast<float2 *>(reinterpret_cast<float *>(a.kv.v) + dst) = make_float2(v0, v1);
+                            *reinterpret_cast<float2 *>(ks) = make_float2(k0, k1);
+                            *reinterpret_cast<float2 *>(vs) = make_float2(v0, v1);
+                        } else {
+                            const __nv_bfloat162 kb = __floats2bfloat162_rn(k0, k1), vb = __floats2bfloat162_rn(v0, v1);
+                            *reinterpret_cast<__nv_bfloat162 *>(reinterpret_cast<__nv_bfloat16 *>(a.kv.k) + dst) = kb;
+                            *reinterpret_cast<__nv_bfloat162 *>(reinterpret_cast<__nv_bfloat16 *>(a.kv.v) + dst) = vb;
+                            *reinterpret_cast<__nv_bfloat162 *>(ks) = kb;
+                            *reinterpret_cast<__nv_bfloat162 *>(vs) = vb;
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
             // ---- S = Q K^T for 16 positions: two n8 tiles ----
             float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
             if constexpr (C::F32) {
@@ -606,7 +682,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     };
     if constexpr (CLU) {
         consume_unit(cu);
-        cluster_epilogue<G, D, C::NW>(a, cu, wm, wl, wo, clb, cx, tid, abort_flag);
+        cluster_epilogue<G, D, C::NW>(a, cu, wm, wl, wo, clb, cx, tid, abort_flag, fz_cs);
         // split-KV across GPUs: this CTA's share of the cross-rank merge (every cluster is
         // resident: the host checks)
         if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);

@@ -194,6 +194,16 @@ struct DecodeArgs {
         int nranks, rank;
         unsigned long long wait_ns;             // limit of each wait for a peer's words
     } px;
+    // A decode step fused into the attention launch (cluster mode only; inactive when k is
+    // null): q [nseq][nHead*D] (a.q points to it) and k [nseq][nHeadKv*D] are rotated at
+    // position pos[b] in place, and the rotated k and v are written into the cache at that
+    // position, in the same kernel -- what launch_rope_append followed by the decode does, with
+    // the same arithmetic.
+    struct Fuse {
+        float *q, *k;
+        const float *v;
+        RopeTab tab;
+    } fz;
 };
 cudaError_t launch_decode(const DecodeArgs &a, int num_ctas, cudaStream_t s);
 // Resident CTAs per SM of the decode kernel a launch for nseq sequences uses.

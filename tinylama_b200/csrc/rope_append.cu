@@ -39,8 +39,7 @@ namespace {
 
 __device__ __forceinline__ void rotate_cs(float x0, float x1, float c, float s, float &y0,
                                           float &y1) {
-    y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    rope_rotate(x0, x1, c, s, y0, y1);
 }
 
 template <typename KV>
@@ -82,11 +81,9 @@ __global__ void rope_append_kernel(const RopeAppendArgs a, const RopeTab tab) {
             const bool rot = i < tab.pairs;
             float c = 1.f, sn = 0.f;
             if (rot) {
-                const float angle = __fmul_rn((float)pos, tab.theta[i]);
-                double sd, cd;
-                sincos((double)angle, &sd, &cd);
-                c = (float)cd;
-                sn = (float)sd;
+                const float2 cs = rope_cos_sin(pos, tab.theta[i]);
+                c = cs.x;
+                sn = cs.y;
             }
             const bool in_range = pos >= 0 && pos < a.kv.maxLen;
             const int h_end = min(hq + hk, (hg + 1) * kHeadsPerThread);
@@ -174,15 +171,7 @@ __global__ void __launch_bounds__(256) rope_append_tok_kernel(const RopeAppendAr
         const int pos = (a.pos0 ? a.pos0[b] : a.pos0_scalar) + t;
         __syncthreads();  // the previous token's cos/sin are no longer read
         for (int i = threadIdx.x; i < half; i += blockDim.x) {
-            float c = 1.f, sn = 0.f;
-            if (i < tab.pairs) {
-                const float angle = __fmul_rn((float)pos, tab.theta[i]);
-                double sd, cd;
-                sincos((double)angle, &sd, &cd);
-                c = (float)cd;
-                sn = (float)sd;
-            }
-            cs[i] = make_float2(c, sn);
+            cs[i] = i < tab.pairs ? rope_cos_sin(pos, tab.theta[i]) : make_float2(1.f, 0.f);
         }
         __syncthreads();
         const bool in_range = pos >= 0 && pos < a.kv.maxLen;
@@ -250,15 +239,7 @@ __global__ void __launch_bounds__(256) rope_append_pos_kernel(const RopeAppendAr
         const int pos = a.pos0_scalar + t;
         __syncthreads();  // the previous position's cos/sin are no longer read
         for (int i = threadIdx.x; i < half; i += blockDim.x) {
-            float c = 1.f, sn = 0.f;
-            if (i < tab.pairs) {
-                const float angle = __fmul_rn((float)pos, tab.theta[i]);
-                double sd, cd;
-                sincos((double)angle, &sd, &cd);
-                c = (float)cd;
-                sn = (float)sd;
-            }
-            cs[i] = make_float2(c, sn);
+            cs[i] = i < tab.pairs ? rope_cos_sin(pos, tab.theta[i]) : make_float2(1.f, 0.f);
         }
         __syncthreads();
         const bool in_range = pos >= 0 && pos < a.kv.maxLen;

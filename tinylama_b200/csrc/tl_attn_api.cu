@@ -220,11 +220,24 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
     return p;
 }
 
+// A decode step (RoPE, append, attention) may run as one launch: when the plan picks cluster
+// mode, the tensor-core kernel rotates q and the new k itself and writes k and v into the cache
+// (DecodeArgs::Fuse).  TL_DECODE_FUSE=0 in a call's environment keeps the two launches.
+bool fuse_allowed() {
+    const char *e = getenv("TL_DECODE_FUSE");
+    return !(e && e[0] == '0');
+}
+
+// rope (optional): the RoPE/append launch of a decode step, fused into the decode launch when
+// the plan allows it, otherwise launched before it.
 int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, const int *pos_host,
                const float *q, float *out, cudaStream_t s, int pos_offset, float *lse_out,
-               const DecodeArgs::Peer *px = nullptr) {
+               const DecodeArgs::Peer *px = nullptr, const RopeAppendArgs *rope = nullptr) {
     Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen, true, px != nullptr);
     TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
+    const RopeTab tab = make_rope_tab(h->ropeDim, h->ropeBase);
+    const bool fused = rope && p.cluster > 0 && !px && !lse_out && pos_offset == 0 && fuse_allowed();
+    if (rope && !fused) TL_CUDA(launch_rope_append(*rope, tab, s));
     DecodeArgs a{};
     a.q = q;
     a.out = out;
@@ -246,9 +259,19 @@ int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, c
     a.lse_out = lse_out;
     if (px) a.px = *px;
     a.cluster = p.cluster;
+    if (fused) {
+        a.fz.q = rope->q.ptr;
+        a.fz.k = rope->k.ptr;
+        a.fz.v = rope->v.ptr;
+        a.fz.tab = tab;
+    }
     cudaError_t e = launch_decode(a, p.ctas, s);
     if (e == cudaErrorNotSupported && p.cluster > 0) {
         // the tensor-core kernel could not be set up: plan again for the CUDA-core kernel
+        if (fused) {
+            a.fz = DecodeArgs::Fuse{};
+            TL_CUDA(launch_rope_append(*rope, tab, s));
+        }
         p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen);
         TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
         a.chunk = p.chunk;
@@ -852,8 +875,7 @@ int tl_decode_step(tl_attn *h, int layer, int slot0, int nseq, const int *pos_de
     a.rope_q = a.rope_k = a.store = true;
     a.layer = layer;
     a.slot0 = slot0;
-    TL_CUDA(launch_rope_append(a, make_rope_tab(h->ropeDim, h->ropeBase), s));
-    return run_decode(h, layer, slot0, nseq, pos_dev, pos_host, q, out, s, 0, nullptr);
+    return run_decode(h, layer, slot0, nseq, pos_dev, pos_host, q, out, s, 0, nullptr, nullptr, &a);
 }
 
 int tl_decode_attention(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev,
