@@ -201,8 +201,15 @@ Plan plan_decode(const tl_attn *h, int nseq, const int *pos_host, int pos_offset
     }
     Plan p{};
     if (cluster_ok && plan_cluster(h, nseq, nmax, tot, ctas, exchange, &p)) return p;
-    long long want = (tot * h->nHeadKv + (long long)ctas * 4 - 1) / ((long long)ctas * 4);
-    int chunk = (int)std::min<long long>(1024, std::max<long long>(32, want));
+    // Chunk length: about `upc` units per CTA, at most 4096 positions.  A unit has a fixed cost
+    // (its q, the merge of the consumer warps and, when a sequence has several chunks, a partial
+    // written and merged again) that outweighs the tail of unevenly finished units: at 256
+    // sequences of L ~ U[256, 4096], 4 units per CTA of at most 1024 positions gave 0.66 of the
+    // HBM peak on the bf16 GQA shape (32/4/64) and one unit per CTA of at most 4096 gave 0.88;
+    // the f32 caches (two CTAs per SM, twice the bytes per position) do best with about three.
+    const int upc = h->kvDtype == TL_KV_BF16 ? 1 : 3;
+    long long want = (tot * h->nHeadKv + (long long)ctas * upc - 1) / ((long long)ctas * upc);
+    int chunk = (int)std::min<long long>(4096, std::max<long long>(32, want));
     chunk = (chunk + 31) / 32 * 32;
     // at most 64 chunks per sequence: the last CTA of a sequence merges all of them
     const int min_chunk = ((nmax + 63) / 64 + 31) / 32 * 32;
