@@ -219,9 +219,9 @@ TL_API int tl_dist_unique_id(char *id128);
  * [rank*maxLen, (rank+1)*maxLen) of every sequence (its slice).  Every rank exports an exchange
  * buffer with CUDA IPC and maps every peer's; NCCL is used here only to pass the IPC handles.
  * If the peers cannot be mapped (or TL_DIST_NCCL=1 is set), the calls below exchange through
- * an NCCL all-gather instead.  If some rank never joins, the call fails with TL_ERR_NCCL after
- * TL_DIST_INIT_TIMEOUT_MS milliseconds (environment; default 120000) instead of waiting for
- * ever.  TL_DIST_WAIT_MS (default 2000) bounds each wait of a split-KV call for a peer's
+ * an NCCL all-gather instead.  With TL_DIST_INIT_TIMEOUT_MS set (environment, milliseconds)
+ * the set-up is non-blocking: if some rank never joins, the call fails with TL_ERR_NCCL after
+ * that time instead of waiting for ever (without it, NCCL's blocking set-up waits for all).  TL_DIST_WAIT_MS (default 2000) bounds each wait of a split-KV call for a peer's
  * values.  TL_DIST_FAULT_SILENT_PEER=1 (test only, one-rank groups) injects a second rank
  * whose values never arrive, so that every call runs into that bound. */
 TL_API int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank);

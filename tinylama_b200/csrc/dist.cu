@@ -108,7 +108,7 @@ long long env_ms(const char *name, long long dflt) {
 // On a non-blocking communicator an NCCL call may return before its work is enqueued: poll
 // until it is, or until the operation fails.  A blocking communicator returns at once.
 ncclResult_t nccl_settle(const tl_attn *h, ncclResult_t r) {
-    if (!nccl().nonblocking || (r != ncclSuccess && r != ncclInProgress)) return r;
+    if (!h->commNonblocking || (r != ncclSuccess && r != ncclInProgress)) return r;
     const auto comm = reinterpret_cast<ncclComm_t>(h->comm);
     ncclResult_t st = ncclInProgress;
     while (true) {
@@ -254,9 +254,11 @@ int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank) {
     memcpy(&id, id128, sizeof id);
     ncclComm_t comm = nullptr;
     ncclResult_t r;
-    if (nccl().nonblocking) {
-        // non-blocking set-up, given up after TL_DIST_INIT_TIMEOUT_MS (default 120 s) if some
-        // rank never joins: the call then fails instead of waiting for ever
+    const bool nonblocking = nccl().nonblocking && env_ms("TL_DIST_INIT_TIMEOUT_MS", 0) > 0;
+    if (nonblocking) {
+        // with TL_DIST_INIT_TIMEOUT_MS set: a non-blocking set-up, given up after that many
+        // milliseconds if some rank never joins, so that the call fails instead of waiting for
+        // ever (without it, NCCL's own blocking set-up)
         ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
         cfg.blocking = 0;
         const long long limit_ms = env_ms("TL_DIST_INIT_TIMEOUT_MS", 120000);
@@ -289,6 +291,7 @@ int tl_dist_init(tl_attn *h, const char *id128, int nranks, int rank) {
     cudaSetDevice(prev);
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
     h->comm = comm;
+    h->commNonblocking = nonblocking;
     h->nranks = nranks;
     h->rank = rank;
     h->epoch = 0;
@@ -356,7 +359,7 @@ void tl_dist_finalize(tl_attn *h) {
         cudaFree(h->dSilentPeer);
         h->dSilentPeer = nullptr;
     }
-    if (nccl().nonblocking) nccl_settle(h, nccl().CommFinalize(reinterpret_cast<ncclComm_t>(h->comm)));
+    if (h->commNonblocking) nccl_settle(h, nccl().CommFinalize(reinterpret_cast<ncclComm_t>(h->comm)));
     nccl().CommDestroy(reinterpret_cast<ncclComm_t>(h->comm));
     cudaSetDevice(prev);
     h->comm = nullptr;

@@ -81,6 +81,7 @@ struct tl_attn {
     cudaEvent_t evIn[4] = {}, evOut[4] = {}, evDone = nullptr;
     // multi-GPU split-KV
     void *comm = nullptr;           // ncclComm_t (used to exchange the IPC handles)
+    bool commNonblocking = false;   // set up non-blocking (TL_DIST_INIT_TIMEOUT_MS)
     int nranks = 1, rank = 0;
     float *dGather = nullptr;
     size_t gatherCap = 0;
