@@ -181,7 +181,10 @@ __device__ __forceinline__ bool word_ready(unsigned long long w, unsigned epoch)
     return (int)((unsigned)(w >> 32) - epoch) >= 0;
 }
 // Re-read a word until it carries this call's epoch, bounded by wait_ns from t0.  Returns the
-// value, or 0 with *ok cleared (and the timeout bit set) on time-out.
+// value, or 0 with *ok cleared (and the timeout bit set) on time-out.  Between reads the thread
+// backs off: every consumer thread of the grid may be waiting here while other CTAs of this
+// rank are still streaming their K/V, and a tight loop of system-scope loads would compete
+// with that stream and with the peers' incoming stores.
 __device__ __forceinline__ float wait_word(const unsigned long long *p, unsigned long long w, unsigned epoch,
                                            uint64_t t0, unsigned long long wait_ns, bool *ok, unsigned *err) {
     while (!word_ready(w, epoch)) {
@@ -191,6 +194,7 @@ __device__ __forceinline__ float wait_word(const unsigned long long *p, unsigned
             *ok = false;
             return 0.f;
         }
+        __nanosleep(128);
         w = ld_word_sys(p);
     }
     return __uint_as_float((unsigned)w);
