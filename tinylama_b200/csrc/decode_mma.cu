@@ -76,8 +76,8 @@ struct MmaCfg {
     static constexpr int OFF_WL = OFF_WM + NW * G * 4;
     static constexpr int OFF_WO = OFF_WL + NW * G * 4;
     static constexpr int OFF_CW = OFF_WO + NW * G * D * 4;
-    static constexpr int OFF_CX = OFF_CW + kMaxChunksPerSeq * G * 4;   // cluster mode: 2 mbarriers,
-    static constexpr int OFF_PREFIX = OFF_CX + 16 + G * (D + 2) * 4;    // then (m, l, o) of this CTA
+    static constexpr int OFF_CX = (OFF_CW + kMaxChunksPerSeq * G * 4 + 15) / 16 * 16;  // cluster mode:
+    static constexpr int OFF_PREFIX = OFF_CX + 16 + G * (D + 2) * 4;  // o (16-B aligned), then (m, l) pairs
     static size_t smem_bytes(int nseq) { return 1024 + (size_t)OFF_PREFIX + 4 * (2 * (size_t)nseq + 1) + 16; }
 };
 
@@ -167,39 +167,25 @@ __device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
     return r;
 }
-__device__ __forceinline__ float ld_cluster(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+// Distributed shared-memory loads of another CTA's (m, l) pair and four o values.  Volatile,
+// so they stay after the cluster barrier, without a memory clobber, so that a thread's loads of
+// all the ranks issue back to back and their latencies overlap.
+__device__ __forceinline__ float2 ld_cluster_v2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
     return v;
 }
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
 }
-// bounded wait with cluster-scope acquire (the arrivals came from other CTAs of the cluster)
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *err,
-                                                  volatile int *abort_flag) {
-    auto test = [&]() {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        return ok != 0;
-    };
-    if (test()) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
-        if (test()) return true;
-        if (abort_flag && *abort_flag) return false;
-        if (globaltimer_ns() - t0 > TL_WAIT_NS) {
-            if (err) atomicOr(err, TL_DEVERR_TIMEOUT);
-            if (abort_flag) *abort_flag = 1;
-            return false;
-        }
-    }
+// The hardware cluster barrier, in its unaligned form (the producer warp's lanes reach it on
+// different paths).  Every thread of every CTA of the cluster reaches each of the two barriers
+// of the epilogue on every path, errors included, so neither can wait for a thread that has left.
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // The merged (O, M, L) of one head element: ctx = O / L, or (O, M, L) to the (o, lse) output,
@@ -217,33 +203,70 @@ __device__ __forceinline__ void cluster_final(const DecodeArgs &a, int b, int he
     }
 }
 
-// End of the unit in cluster mode (the NW*32 consumer threads): this CTA's (m, l, o) for the G
-// heads go to its own shared memory; the CL-1 other CTAs then arrive on rank 0's barrier, rank 0
-// reads their values through distributed shared memory, merges
-//   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L
-// into out, and releases each of them (their shared memory must stay until it has read it).
-// Every wait is bounded, and every CTA arrives whatever its own state, so none waits for ever.
-// Fused decode step: the rotated q of the cluster's G heads written back into the input, by
-// rank 0 once every CTA of the cluster has read q (the tl_decode_step contract rotates q in place).
+// Fused decode step: the cluster's G heads of q are rotated in place (the tl_decode_step
+// contract), but only once every CTA of the cluster has read q.  Each CTA writes the groups of
+// four q values it also merges (at most two per thread), from a copy loaded at the start.
+template <int G, int D>
+struct QStash {
+    static constexpr int MAXG = (G * D / 4 + 127) / 128;  // groups per thread with one CTA
+    float4 v[MAXG];
+};
+// first group and group count of this CTA's share: G*D/4 groups of four values split over CL
+template <int G, int D>
+__device__ __forceinline__ void cluster_share(uint32_t CL, uint32_t rank, int &j0, int &j1) {
+    constexpr int E4 = G * D / 4;
+    const int per = (E4 + (int)CL - 1) / (int)CL;
+    j0 = min(E4, (int)rank * per);
+    j1 = min(E4, j0 + per);
+}
 template <int G, int D, int NW>
-__device__ __forceinline__ void fuse_write_q(const DecodeArgs &a, const Unit &un, const float2 *cs, int tid) {
-    for (int e = 2 * tid; e < G * D; e += 2 * NW * 32) {
-        const int h = e / D, dd = e - h * D, i = dd >> 1;
-        if (i >= a.fz.tab.pairs) continue;
-        const int64_t idx = ((int64_t)un.b * a.nHead + un.g * G + h) * D + dd;
-        float x0 = a.fz.q[idx], x1 = a.fz.q[idx + 1];
-        rope_rotate(x0, x1, cs[i].x, cs[i].y, x0, x1);
-        a.fz.q[idx] = x0;
-        a.fz.q[idx + 1] = x1;
+__device__ __forceinline__ void q_stash_load(const DecodeArgs &a, const Unit &un, QStash<G, D> &qs, int tid) {
+    int j0, j1;
+    cluster_share<G, D>(cluster_size(), cluster_rank(), j0, j1);
+#pragma unroll
+    for (int k = 0; k < QStash<G, D>::MAXG; ++k) {
+        const int j = j0 + tid + k * NW * 32;
+        if (j < j1) {
+            const int e = 4 * j, h = e / D, dd = e - h * D;
+            qs.v[k] = *reinterpret_cast<const float4 *>(a.fz.q + ((int64_t)un.b * a.nHead + un.g * G + h) * D + dd);
+        }
+    }
+}
+template <int G, int D, int NW>
+__device__ __forceinline__ void q_stash_write(const DecodeArgs &a, const Unit &un, const QStash<G, D> &qs,
+                                              const float2 *cs, int tid) {
+    int j0, j1;
+    cluster_share<G, D>(cluster_size(), cluster_rank(), j0, j1);
+#pragma unroll
+    for (int k = 0; k < QStash<G, D>::MAXG; ++k) {
+        const int j = j0 + tid + k * NW * 32;
+        if (j < j1) {
+            const int e = 4 * j, h = e / D, dd = e - h * D, i = dd >> 1;
+            float4 x = qs.v[k];
+            if (i < a.fz.tab.pairs) rope_rotate(x.x, x.y, cs[i].x, cs[i].y, x.x, x.y);
+            if (i + 1 < a.fz.tab.pairs) rope_rotate(x.z, x.w, cs[i + 1].x, cs[i + 1].y, x.z, x.w);
+            *reinterpret_cast<float4 *>(a.fz.q + ((int64_t)un.b * a.nHead + un.g * G + h) * D + dd) = x;
+        }
     }
 }
 
+// End of the unit in cluster mode, run by the NW*32 consumer threads (the producer warp meets
+// them at the two cluster barriers: producer_cluster_barriers).
+//  1. The warps' (m, l, o) are merged into this CTA's own (cm, cl) pairs and co row.
+//  2. Cluster barrier: every CTA's values are in its shared memory (and every CTA has read q).
+//  3. CTA `rank` merges its 1/CL share of the G*D elements from all CTAs of the cluster through
+//     distributed shared memory,
+//       M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L,
+//     with a thread's loads of every rank issued back to back, and writes that share of ctx (and
+//     of the rotated q for a fused step).
+//  4. Cluster barrier: no CTA leaves while another may still read its shared memory.
 template <int G, int D, int NW>
 __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit &un, const float *wm, const float *wl,
-                                                 const float *wo, uint64_t *clb, float *cx, int tid,
-                                                 volatile int *abort_flag, const float2 *fz_cs) {
+                                                 const float *wo, float *cx, int tid, const QStash<G, D> &qst,
+                                                 const float2 *fz_cs) {
     named_bar(1, NW * 32);
-    float *cm = cx, *cl = cx + G, *co = cx + 2 * G;
+    float *co = cx;                                       // [G*D], 16-byte aligned
+    float2 *cml = reinterpret_cast<float2 *>(cx + G * D);  // [G] (m, l)
     for (int e = tid; e < G * D; e += NW * 32) {
         const int h = e / D, dd = e - h * D;
         float M = -INFINITY;
@@ -257,54 +280,61 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
             O = fmaf(wo[(w * G + h) * D + dd], sw, O);
         }
         co[e] = O;
-        if (dd == 0) { cm[h] = M; cl[h] = L; }
+        if (dd == 0) cml[h] = make_float2(M, L);
     }
-    asm volatile("fence.acq_rel.cluster;" ::: "memory");
-    named_bar(1, NW * 32);
     const uint32_t CL = cluster_size(), rank = cluster_rank();
-    if (CL == 1) {
-        for (int e = tid; e < G * D; e += NW * 32) {
-            const int h = e / D, dd = e - h * D;
-            cluster_final<D>(a, un.b, un.g * G + h, dd, co[e], cm[h], cl[h]);
-        }
-        if (a.fz.k != nullptr) fuse_write_q<G, D, NW>(a, un, fz_cs, tid);
-        return;
-    }
-    if (rank != 0) {
-        if (tid == 0) mbar_arrive_remote(cluster_addr(&clb[0], 0));
-        // not cut short by this CTA's own abort: rank 0 may still be reading this shared memory
-        __all_sync(0xffffffffu, mbar_wait_cluster(&clb[1], 0, a.err, nullptr));
-        return;
-    }
-    const bool ok = __all_sync(0xffffffffu, mbar_wait_cluster(&clb[0], 0, a.err, abort_flag));
-    // every CTA of the cluster has arrived, so every one has read q
-    if (ok && a.fz.k != nullptr) fuse_write_q<G, D, NW>(a, un, fz_cs, tid);
-    if (ok) {
-        for (int e = tid; e < G * D; e += NW * 32) {
-            const int h = e / D, dd = e - h * D;
-            float m[kMaxCluster], l[kMaxCluster], o[kMaxCluster];
-            float M = -INFINITY;
+    named_bar(1, NW * 32);
+    if (CL > 1) cluster_barrier();
+    int j0, j1;
+    cluster_share<G, D>(CL, rank, j0, j1);
+    for (int j = j0 + tid; j < j1; j += NW * 32) {
+        const int e = 4 * j, h = e / D, dd = e - h * D;
+        float2 ml[kMaxCluster];
+        float4 o4[kMaxCluster];
+        if (CL == 1) {
+            ml[0] = cml[h];
+            o4[0] = *reinterpret_cast<const float4 *>(co + e);
+        } else {
 #pragma unroll
             for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r) {
-                if (r >= CL) break;
-                m[r] = ld_cluster(cluster_addr(&cm[h], r));
-                l[r] = ld_cluster(cluster_addr(&cl[h], r));
-                o[r] = ld_cluster(cluster_addr(&co[e], r));
-                M = fmaxf(M, m[r]);
+                if (r < CL) {
+                    ml[r] = ld_cluster_v2(cluster_addr(&cml[h], r));
+                    o4[r] = ld_cluster_v4(cluster_addr(co + e, r));
+                }
             }
-            float L = 0.f, O = 0.f;
-#pragma unroll
-            for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r) {
-                if (r >= CL) break;
-                const float w = safe_exp2_diff(m[r], M);
-                L = fmaf(l[r], w, L);
-                O = fmaf(o[r], w, O);
-            }
-            cluster_final<D>(a, un.b, un.g * G + h, dd, O, M, L);
         }
+        float M = -INFINITY;
+#pragma unroll
+        for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r)
+            if (r < CL) M = fmaxf(M, ml[r].x);
+        float L = 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r) {
+            if (r < CL) {
+                const float w = safe_exp2_diff(ml[r].x, M);
+                L = fmaf(ml[r].y, w, L);
+                O.x = fmaf(o4[r].x, w, O.x);
+                O.y = fmaf(o4[r].y, w, O.y);
+                O.z = fmaf(o4[r].z, w, O.z);
+                O.w = fmaf(o4[r].w, w, O.w);
+            }
+        }
+        const int head = un.g * G + h;
+        cluster_final<D>(a, un.b, head, dd, O.x, M, L);
+        cluster_final<D>(a, un.b, head, dd + 1, O.y, M, L);
+        cluster_final<D>(a, un.b, head, dd + 2, O.z, M, L);
+        cluster_final<D>(a, un.b, head, dd + 3, O.w, M, L);
     }
-    named_bar(1, NW * 32);  // rank 0 has read every CTA's values
-    if (tid >= 1 && tid < (int)CL) mbar_arrive_remote(cluster_addr(&clb[1], (uint32_t)tid));
+    if (a.fz.k != nullptr) q_stash_write<G, D, NW>(a, un, qst, fz_cs, tid);
+    if (CL > 1) cluster_barrier();
+}
+// the producer warp's part of the epilogue: the same two cluster barriers
+__device__ __forceinline__ void producer_cluster_barriers() {
+    if (cluster_size() > 1) {
+        cluster_barrier();
+        cluster_barrier();
+    }
 }
 
 template <typename KV, int D, int G, bool CLU>
@@ -327,8 +357,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     int *prefix = reinterpret_cast<int *>(smem + C::OFF_PREFIX);
     int *lens = prefix + (a.nseq + 1);
     UnitQueue *uq = reinterpret_cast<UnitQueue *>(smem + C::OFF_UQ);
-    uint64_t *clb = reinterpret_cast<uint64_t *>(smem + C::OFF_CX);  // cluster mode: [0] gather, [1] release
-    float *cx = reinterpret_cast<float *>(smem + C::OFF_CX + 16);
+    float *cx = reinterpret_cast<float *>(smem + C::OFF_CX + 16);  // cluster mode: this CTA's (o, m, l)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned *err = a.err;
@@ -341,16 +370,17 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             mbar_init(&uq->full[s], 1);
             mbar_init(&uq->empty[s], C::NW);
         }
-        if constexpr (CLU) {
-            const int cl = (int)cluster_size();
-            mbar_init(&clb[0], cl > 1 ? cl - 1 : 1);  // the other CTAs of the cluster
-            mbar_init(&clb[1], 1);                    // rank 0, done reading
-        }
         *abort_flag = 0;
         fence_mbar_init();
     }
     // cluster mode: every CTA's barriers exist before any CTA arrives on them
     if constexpr (CLU) cluster_sync_all();
+    // a fused decode step: this thread's RoPE frequency (a table of the handle, written by no
+    // kernel) is fetched before the wait
+    static_assert(D / 2 <= C::NW * 32, "one RoPE pair per consumer thread");
+    const bool fuse = CLU && a.fz.k != nullptr;
+    float fz_theta = 0.f;
+    if (fuse && tid < D / 2 && tid < a.fz.tab.pairs) fz_theta = a.fz.tab.theta[tid];
     // launched behind the RoPE/append kernel: positions, q and the cache are read after it
     pdl_wait();
     // a kernel launched behind this one with programmatic serialisation may start its own
@@ -383,14 +413,15 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
         // device would leave positions past the cluster's last chunk unread
         if (tid == 0 && rank == cl - 1 && (long long)cu.n > (long long)cl * a.chunk) atomicOr(err, TL_DEVERR_BAD_ARG);
     }
-    // a decode step fused into this launch (cluster mode): the cos/sin of this sequence's
-    // position, for the rotation of q (every CTA) and of the new k (the CTA whose chunk holds it)
+    // a decode step fused into this launch (cluster mode): this CTA's share of q for the in-place
+    // rotation at the end, then the cos/sin of this sequence's position, for the rotation of q
+    // (every CTA) and of the new k (the CTA whose chunk holds it)
     __shared__ float2 fz_cs[64];
-    const bool fuse = CLU && a.fz.k != nullptr;
+    QStash<G, D> qst;
+    if (fuse && warp < C::NW) q_stash_load<G, D, C::NW>(a, cu, qst, tid);
     const int fz_pos = fuse ? a.pos[cu.b] : -1;
     if (fuse && warp < C::NW) {
-        for (int i = tid; i < D / 2; i += C::NW * 32)
-            fz_cs[i] = i < a.fz.tab.pairs ? rope_cos_sin(fz_pos, a.fz.tab.theta[i]) : make_float2(1.f, 0.f);
+        if (tid < D / 2) fz_cs[tid] = tid < a.fz.tab.pairs ? rope_cos_sin(fz_pos, fz_theta) : make_float2(1.f, 0.f);
         named_bar(1, C::NW * 32);
     }
 
@@ -441,6 +472,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                 mbar_wait(&full[s], ph, err, nullptr);
             }
         }
+        if constexpr (CLU) producer_cluster_barriers();
         return;
     }
 
@@ -682,7 +714,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     };
     if constexpr (CLU) {
         consume_unit(cu);
-        cluster_epilogue<G, D, C::NW>(a, cu, wm, wl, wo, clb, cx, tid, abort_flag, fz_cs);
+        cluster_epilogue<G, D, C::NW>(a, cu, wm, wl, wo, cx, tid, qst, fz_cs);
         // split-KV across GPUs: this CTA's share of the cross-rank merge (every cluster is
         // resident: the host checks)
         if (a.px.nranks > 0 && *abort_flag == 0) peer_merge_pairs<G, D, C::NW>(a, tid);
