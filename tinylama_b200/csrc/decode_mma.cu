@@ -384,8 +384,12 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     // launched behind the RoPE/append kernel: positions, q and the cache are read after it
     pdl_wait();
     // a kernel launched behind this one with programmatic serialisation may start its own
-    // independent prologue (it waits for this grid's completion before reading its output)
-    pdl_launch_dependents();
+    // independent prologue (it waits for this grid's completion before reading its output).
+    // Not with a split-KV exchange: there the next call's clusters, placed while this grid's
+    // merging CTAs still hold their slots, left a cluster without room until the first ones
+    // ended (a second wave of ~20 us at 16384 positions per GPU); the next call then starts
+    // when this grid ends.
+    if (a.px.nranks == 0) pdl_launch_dependents();
     int total_units = 0;
     Unit cu{};
     if constexpr (!CLU) {
