@@ -397,17 +397,23 @@ int ensure_copy_streams(tl_attn *h) {
     return TL_OK;
 }
 
-// Split a batch into `parts` runs of consecutive sequences with about equal KV bytes (the
-// attention time of a part follows its K/V bytes).  cut[j] .. cut[j+1] is part j.
+// Split a batch into `parts` runs of consecutive sequences by their KV bytes (the attention
+// time of a part follows its K/V bytes).  cut[j] .. cut[j+1] is part j.  Two parts are equal.
+// Four parts take 1/8, 3/8, 3/8 and 1/8: only the copy in of the first part and the copy out of
+// the last one are not hidden behind attention, so those two parts are the small ones.
 int split_by_kv(const int *pos, int nseq, int parts, int *cut) {
     long long tot = 0;
     for (int b = 0; b < nseq; ++b) tot += pos[b] + 1;
+    static const int kEnd4[4] = {1, 4, 7, 8};  // cumulative eighths
+    auto reached = [&](long long acc, int j) {
+        return parts == 4 ? acc * 8 >= tot * kEnd4[j - 1] : acc * parts >= tot * j;
+    };
     int j = 1;
     long long acc = 0;
     cut[0] = 0;
     for (int b = 0; b < nseq && j < parts; ++b) {
         acc += pos[b] + 1;
-        if (acc * parts >= tot * j) cut[j++] = b + 1;
+        while (j < parts && reached(acc, j)) cut[j++] = b + 1;
     }
     while (j < parts) cut[j++] = nseq;
     cut[parts] = nseq;
