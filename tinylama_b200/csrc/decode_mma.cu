@@ -147,7 +147,7 @@ __device__ __forceinline__ uint32_t swz(uint32_t box, int row, int chunk) {
 }
 
 // ---- cluster mode: one cluster of CL CTAs per (sequence, kv-head), merged in shared memory ----
-constexpr int kMaxCluster = 8;  // portable cluster size
+constexpr int kMaxCluster = 16;  // 8 is the portable size; 16 with the non-portable attribute
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -289,36 +289,47 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
     cluster_share<G, D>(CL, rank, j0, j1);
     for (int j = j0 + tid; j < j1; j += NW * 32) {
         const int e = 4 * j, h = e / D, dd = e - h * D;
-        float2 ml[kMaxCluster];
-        float4 o4[kMaxCluster];
-        if (CL == 1) {
-            ml[0] = cml[h];
-            o4[0] = *reinterpret_cast<const float4 *>(co + e);
-        } else {
+        // the ranks in groups of 8 (registers), merged online: one group for clusters of up to 8
+        constexpr int RG = 8;
+        float M = -INFINITY, L = 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t r0 = 0; r0 < CL; r0 += RG) {
+            float2 ml[RG];
+            float4 o4[RG];
+            if (CL == 1) {
+                ml[0] = cml[h];
+                o4[0] = *reinterpret_cast<const float4 *>(co + e);
+            } else {
 #pragma unroll
-            for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r) {
-                if (r < CL) {
-                    ml[r] = ld_cluster_v2(cluster_addr(&cml[h], r));
-                    o4[r] = ld_cluster_v4(cluster_addr(co + e, r));
+                for (uint32_t r = 0; r < (uint32_t)RG; ++r) {
+                    if (r0 + r < CL) {
+                        ml[r] = ld_cluster_v2(cluster_addr(&cml[h], r0 + r));
+                        o4[r] = ld_cluster_v4(cluster_addr(co + e, r0 + r));
+                    }
                 }
             }
-        }
-        float M = -INFINITY;
+            float Mn = M;
 #pragma unroll
-        for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r)
-            if (r < CL) M = fmaxf(M, ml[r].x);
-        float L = 0.f;
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (uint32_t r = 0; r < (uint32_t)RG; ++r)
+                if (r0 + r < CL) Mn = fmaxf(Mn, ml[r].x);
+            const float sc = safe_exp2_diff(M, Mn);
+            L *= sc;
+            O.x *= sc;
+            O.y *= sc;
+            O.z *= sc;
+            O.w *= sc;
 #pragma unroll
-        for (uint32_t r = 0; r < (uint32_t)kMaxCluster; ++r) {
-            if (r < CL) {
-                const float w = safe_exp2_diff(ml[r].x, M);
-                L = fmaf(ml[r].y, w, L);
-                O.x = fmaf(o4[r].x, w, O.x);
-                O.y = fmaf(o4[r].y, w, O.y);
-                O.z = fmaf(o4[r].z, w, O.z);
-                O.w = fmaf(o4[r].w, w, O.w);
+            for (uint32_t r = 0; r < (uint32_t)RG; ++r) {
+                if (r0 + r < CL) {
+                    const float w = safe_exp2_diff(ml[r].x, Mn);
+                    L = fmaf(ml[r].y, w, L);
+                    O.x = fmaf(o4[r].x, w, O.x);
+                    O.y = fmaf(o4[r].y, w, O.y);
+                    O.z = fmaf(o4[r].z, w, O.z);
+                    O.w = fmaf(o4[r].w, w, O.w);
+                }
             }
+            M = Mn;
         }
         const int head = un.g * G + h;
         cluster_final<D>(a, un.b, head, dd, O.x, M, L);
@@ -792,6 +803,10 @@ cudaError_t launch_t(const DecodeArgs &a, int num_ctas, cudaStream_t s) {
         auto kern = decode_mma_kernel<KV, D, G, true>;
         cudaError_t e = ensure_smem(kern, smem_set_clu);
         if (e != cudaSuccess) return e;
+        if (a.cluster > 8) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return e;
+        }
         return launch_pdl_cluster(kern, dim3(num_ctas), dim3(C::THREADS), smem, a.cluster, s, km, vm, a);
     }
     static size_t smem_set[64] = {};
@@ -858,6 +873,10 @@ int cluster_capacity_t(int cluster) {
     const size_t smem = C::smem_bytes(512);  // at least what a cluster-mode launch uses (nseq <= 512)
     auto kern = decode_mma_kernel<KV, D, G, true>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    if (cluster > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(cluster);
     cfg.blockDim = dim3(C::THREADS);

@@ -175,11 +175,12 @@ bool plan_cluster(const tl_attn *h, int nseq, int nmax, long long tot, int ctas,
     if (!short_seqs && !(uniform && fills)) return false;
     if (exchange && grid / cl > decode_mma_cluster_capacity(h->headDim, G, h->kvDtype, cl)) return false;
     if (short_seqs && !exchange) {
-        // few short sequences are latency-bound: spread each over up to 8 CTAs of 128 positions
-        // (two tiles, both in flight at once) when that many fit (TinyLlama batch 1 at L = 512:
-        // 10.0 -> 9.4 us per step; clusters of 16, a non-portable size, were slower at L = 2048)
-        constexpr int kShortTarget = 128;
-        const int cl2 = std::min(kMaxCl, std::max(cl, (nmax + kShortTarget - 1) / kShortTarget));
+        // few short sequences are latency-bound: spread each over up to 16 CTAs of 128 positions
+        // (two tiles, both in flight at once) when that many fit; clusters of more than 8 (a
+        // non-portable size) only where the device can hold one
+        constexpr int kShortTarget = 128, kShortMaxCl = 16;
+        int cl2 = std::min(kShortMaxCl, std::max(cl, (nmax + kShortTarget - 1) / kShortTarget));
+        if (cl2 > kMaxCl && decode_mma_cluster_capacity(h->headDim, G, h->kvDtype, cl2) < 1) cl2 = kMaxCl;
         if (cl2 > cl) {
             long long chunk2 = (nmax + cl2 - 1) / cl2;
             chunk2 = std::max<long long>(kTile, (chunk2 + kTile - 1) / kTile * kTile);
