@@ -403,6 +403,26 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     if (a.px.nranks == 0) pdl_launch_dependents();
     int total_units = 0;
     Unit cu{};
+    // producer state (lane 0 of warp NW): ring stage and phase, copies issued
+    int pstage = 0, pspec = 0;
+    uint32_t pphase = 0;
+    long pissued = 0;
+    const uint64_t pol = policy_evict_first();
+    // one K/V tile (positions p .. p+T of the rows from row0) into the next stage of the ring
+    auto issue_tile = [&](int row0, int p) {
+        uint8_t *st = smem + C::OFF_STAGES + pstage * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[pstage], C::STAGE_BYTES);
+#pragma unroll
+        for (int hh = 0; hh < C::HALVES; ++hh) {
+            tma_load_2d(st + hh * C::HALF_BYTES, &kmap, C::BOX_COLS * hh, row0 + p, &full[pstage], pol);
+            tma_load_2d(st + C::TILE_BYTES + hh * C::HALF_BYTES, &vmap, C::BOX_COLS * hh, row0 + p, &full[pstage], pol);
+        }
+        ++pissued;
+        if (++pstage == C::NS) { pstage = 0; pphase ^= 1u; }
+    };
+    const int gid = lane >> 2, tq = lane & 3;  // fragment row (head) and column pair
+    const bool row_ok = gid < G;
+    float4 qpre[C::KT];  // cluster mode: this lane's q values, loaded before the position is known
     if constexpr (!CLU) {
         if (warp == 0) build_schedule(a, prefix, lens, max_nch, lane, err);
         __syncthreads();
@@ -421,6 +441,29 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
         cu.g = pair - cu.b * a.nHeadKv;
         cu.c = rank;
         cu.nch = cl;
+        // Before the position is read, the producer starts the chunk's first tiles (at most the
+        // ring's depth, into stages that start free) and the consumers load their q values.  A
+        // chunk that turns out shorter leaves tiles unconsumed; the producer still waits for them.
+        if (warp == C::NW && lane == 0) {
+            const int row0 = (int)a.kv.row(a.layer, a.slot0 + cu.b, cu.g, 0);
+            for (; pspec < C::NS && pspec * C::T < a.chunk; ++pspec) issue_tile(row0, rank * a.chunk + pspec * C::T);
+        }
+        if (warp < C::NW) {
+            const float *qrow = a.q + ((int64_t)cu.b * a.nHead + (int64_t)cu.g * G + (row_ok ? gid : 0)) * D;
+#pragma unroll
+            for (int kt = 0; kt < C::KT; ++kt) {
+                qpre[kt] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (row_ok) {
+                    if constexpr (C::F32) {
+                        qpre[kt] = *reinterpret_cast<const float4 *>(qrow + 32 * (kt >> 1) + 4 * (2 * tq + (kt & 1)));
+                    } else {
+                        const float2 lo = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq);
+                        const float2 hi = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq + 8);
+                        qpre[kt] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                    }
+                }
+            }
+        }
         cu.n = local_len(a, cu.b, err);
         cu.p0 = min(rank * a.chunk, cu.n);
         cu.p1 = min(cu.p0 + a.chunk, cu.n);
@@ -443,30 +486,17 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     if (warp == C::NW) {
         // ================= producer =================
         if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            int stage = 0;
-            uint32_t phase = 0;
-            long issued = 0;
             bool ok = true;
-            // the copies of one unit's tiles into the ring
-            auto issue_unit = [&](const Unit &un) {
+            // the copies of one unit's tiles into the ring, from its tile `skip` on
+            auto issue_unit = [&](const Unit &un, int skip) {
                 const int row0 = (int)a.kv.row(a.layer, a.slot0 + un.b, un.g, 0);
-                for (int p = un.p0; p < un.p1; p += C::T) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, abort_flag)) { ok = false; break; }
-                    uint8_t *st = smem + C::OFF_STAGES + stage * C::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-#pragma unroll
-                    for (int hh = 0; hh < C::HALVES; ++hh) {
-                        tma_load_2d(st + hh * C::HALF_BYTES, &kmap, C::BOX_COLS * hh, row0 + p, &full[stage], pol);
-                        tma_load_2d(st + C::TILE_BYTES + hh * C::HALF_BYTES, &vmap, C::BOX_COLS * hh, row0 + p,
-                                    &full[stage], pol);
-                    }
-                    ++issued;
-                    if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+                for (int p = un.p0 + skip * C::T; p < un.p1; p += C::T) {
+                    if (!mbar_wait(&empty[pstage], pphase ^ 1u, err, abort_flag)) { ok = false; break; }
+                    issue_tile(row0, p);
                 }
             };
             if constexpr (CLU) {
-                issue_unit(cu);
+                issue_unit(cu, pspec);
             } else {
                 int qs = 0, u = 0;
                 uint32_t qp = 0;
@@ -474,14 +504,14 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                 while (ok) {
                     if (!unitq_push(a, uq, prefix, total_units, qs, qp, u, first, err, abort_flag)) { ok = false; break; }
                     if (u < 0) break;
-                    issue_unit(decode_unit(a, prefix, lens, u));
+                    issue_unit(decode_unit(a, prefix, lens, u), 0);
                 }
             }
             if (!CLU && ok) unitq_finish(a);
             // wait (bounded) for every copy issued into this CTA's shared memory
-            const int outstanding = issued < (long)C::NS ? (int)issued : C::NS;
-            int s = stage;
-            uint32_t ph = phase;
+            const int outstanding = pissued < (long)C::NS ? (int)pissued : C::NS;
+            int s = pstage;
+            uint32_t ph = pphase;
             for (int i = 0; i < outstanding; ++i) {
                 if (--s < 0) { s = C::NS - 1; ph ^= 1u; }
                 mbar_wait(&full[s], ph, err, nullptr);
@@ -492,8 +522,6 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
     }
 
     // ================= consumers =================
-    const int gid = lane >> 2, tq = lane & 3;  // fragment row (head) and column pair
-    const bool row_ok = gid < G;
     const float C2 = kLog2e / sqrtf((float)D);
     int stage = 0;
     uint32_t phase = 0;
@@ -510,7 +538,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
             for (int kt = 0; kt < C::KT; ++kt) {
                 if constexpr (C::F32) {
                     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (row_ok) x = *reinterpret_cast<const float4 *>(qrow + 32 * (kt >> 1) + 4 * (2 * tq + (kt & 1)));
+                    if constexpr (CLU) x = qpre[kt];
+                    else if (row_ok) x = *reinterpret_cast<const float4 *>(qrow + 32 * (kt >> 1) + 4 * (2 * tq + (kt & 1)));
                     if (fuse) {  // columns c, c+1 and c+2, c+3: pairs c/2 and c/2 + 1
                         const int pr0 = 16 * (kt >> 1) + 2 * (2 * tq + (kt & 1));
                         if (pr0 < a.fz.tab.pairs) rope_rotate(x.x, x.y, fz_cs[pr0].x, fz_cs[pr0].y, x.x, x.y);
@@ -522,7 +551,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constan
                     split_tf32(x.w, qh[kt][3], ql[kt][3]);
                 } else {
                     float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
-                    if (row_ok) {
+                    if constexpr (CLU) {
+                        x0 = qpre[kt].x; x1 = qpre[kt].y; x2 = qpre[kt].z; x3 = qpre[kt].w;
+                    } else if (row_ok) {
                         const float2 lo = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq);
                         const float2 hi = *reinterpret_cast<const float2 *>(qrow + 16 * kt + 2 * tq + 8);
                         x0 = lo.x; x1 = lo.y; x2 = hi.x; x3 = hi.y;
