@@ -161,6 +161,45 @@ __device__ __forceinline__ void q2_compute(const Q2Part &p, int n, int h, const 
     }
 }
 
+// One token (the decode step): the same sums with two weights per packed multiply-add
+// (fma.rn.f32x2: even and odd weights in two partial sums, added at the end of the sub-block),
+// and the float 1 + q/4 of each weight made by one byte permutation from a word that holds four
+// weights' bytes 0x80 | q << 5 (a shift and two logic ops per four weights).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long *>(&a)), "l"(*reinterpret_cast<unsigned long long *>(&b)),
+          "l"(*reinterpret_cast<unsigned long long *>(&c)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+__device__ __forceinline__ void q2_compute1(const Q2Part &p, int n, int h, const float *xs, const float *xsum,
+                                            int base, float &acc) {
+    const float d = h2f(p.dd & 0xFFFFu), dmin = h2f(p.dd >> 16);
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const uint32_t word = it < 2 ? p.sa : p.sb;
+        const uint32_t sc = (word >> (8 * (2 * (it & 1) + h))) & 0xFFu;
+        const float dl = __fmul_rn(d, (float)(sc & 15u)), ml = __fmul_rn(dmin, (float)(sc >> 4));
+        const int w0 = base + 128 * n + 32 * it + 16 * h;  // first weight of the sub-block
+        float2 F = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // weights 4c .. 4c+3: bytes of q[c]
+            const uint32_t T = (((p.q[c] >> (2 * it)) & 0x03030303u) << 5) | 0x80808080u;
+            const float4 xv = *reinterpret_cast<const float4 *>(xs + xpad(w0 + 4 * c));
+            // bytes (0, 0, 0x80 | q << 5, 0x3F): the float 1 + q/4
+            const float f0 = __uint_as_float(__byte_perm(T, 0x3F00u, 0x5044u));
+            const float f1 = __uint_as_float(__byte_perm(T, 0x3F00u, 0x5144u));
+            const float f2 = __uint_as_float(__byte_perm(T, 0x3F00u, 0x5244u));
+            const float f3 = __uint_as_float(__byte_perm(T, 0x3F00u, 0x5344u));
+            F = ffma2(make_float2(f0, f1), make_float2(xv.x, xv.y), F);
+            F = ffma2(make_float2(f2, f3), make_float2(xv.z, xv.w), F);
+        }
+        const float X = xsum[w0 >> 4];
+        acc = fmaf(dl, 4.f * ((F.x + F.y) - X), fmaf(-ml, X, acc));
+    }
+}
+
 template <int NS>
 __device__ __forceinline__ void row_dot(const GMat &M, int row, int in, const float *xs, int xstride,
                                         const float *xsum, int sstride, int S, int lane, float *acc) {
@@ -426,8 +465,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q2k_kernel(const GemvArgs a,
                     const int t = lane + 32 * k;
                     if (t < ntask) {
                         const int n = (t >> 1) & 1, h = t & 1, base = (t >> 2) * QK;
-                        q2_compute<NS>(buf[jj][r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, acc[r]);
-                        if (SWI) q2_compute<NS>(buf[jj][RP * TPL + r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, up[r]);
+                        if constexpr (NS == 1) {
+                            q2_compute1(buf[jj][r * TPL + k], n, h, xs, xsum, base, acc[r][0]);
+                            if (SWI) q2_compute1(buf[jj][RP * TPL + r * TPL + k], n, h, xs, xsum, base, up[r][0]);
+                        } else {
+                            q2_compute<NS>(buf[jj][r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, acc[r]);
+                            if (SWI) q2_compute<NS>(buf[jj][RP * TPL + r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, up[r]);
+                        }
                     }
                 }
             }
