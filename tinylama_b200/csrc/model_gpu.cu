@@ -234,7 +234,10 @@ __device__ __forceinline__ void row_dot(const GMat &M, int row, int in, const fl
 // The block's copy of x in shared memory: normalised (rmsnormCols) when a.norm is set, and the
 // sums of its 16-element sub-blocks.  Each thread loads its share of a token's x (and of the
 // norm weights) as float4s in one batch, so the row costs one round trip to L2, not one per
-// element.  V4 float4s per thread: inputs up to V4 * 1024 wide.  Ends with a barrier.
+// element.  The norm's sum of squares takes one barrier per token (red holds every token's
+// warp partials, each thread adds the 8 of its token); a sub-block's sum is formed in
+// registers by the four lanes that hold its float4s.  V4 float4s per thread: inputs up to
+// V4 * 1024 wide.  red: kMaxS * 8 floats.  Ends with a barrier.
 constexpr int kMaxIn = 8192;
 constexpr int kV4 = kMaxIn / 4 / kThreads;  // float4s per thread at the widest input
 
@@ -269,22 +272,19 @@ __device__ __forceinline__ void stage_x(const GemvArgs &a, float *xs, float *xsu
                 }
             }
             ss = warp_sum(ss);
-            if (lane == 0) red[warp] = ss;
+            if (lane == 0) red[s * (kThreads / 32) + warp] = ss;
             __syncthreads();
-            if (warp == 0) {
-                float t = lane < kThreads / 32 ? red[lane] : 0.f;
-                t = warp_sum(t);
-                if (lane == 0) red[0] = t;
-            }
-            __syncthreads();
-            inv = 1.f / sqrtf(red[0] / (float)a.in + a.eps);
-            __syncthreads();  // red is reused by the next token
+            float t = 0.f;
+#pragma unroll
+            for (int i = 0; i < kThreads / 32; ++i) t += red[s * (kThreads / 32) + i];
+            inv = 1.f / sqrtf(t / (float)a.in + a.eps);
         }
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
             const int i4 = tid + k * kThreads;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
             if (i4 < n4) {
-                float4 o = v[k];
+                o = v[k];
                 if (a.norm) {
                     o.x = __fmul_rn(__fmul_rn(o.x, inv), w[k].x);
                     o.y = __fmul_rn(__fmul_rn(o.y, inv), w[k].y);
@@ -293,19 +293,12 @@ __device__ __forceinline__ void stage_x(const GemvArgs &a, float *xs, float *xsu
                 }
                 *reinterpret_cast<float4 *>(xs + s * xstride + xpad(4 * i4)) = o;
             }
+            // the sub-block of float4s 4j .. 4j+3 sits in four consecutive lanes
+            float t = (o.x + o.y) + (o.z + o.w);
+            t += __shfl_xor_sync(0xffffffffu, t, 1);
+            t += __shfl_xor_sync(0xffffffffu, t, 2);
+            if ((lane & 3) == 0 && (i4 >> 2) < sstride) xsum[s * sstride + (i4 >> 2)] = t;
         }
-    }
-    __syncthreads();
-    for (int e = tid; e < a.S * sstride; e += kThreads) {
-        const int s = e / sstride, j = e - s * sstride;
-        const float4 *p = reinterpret_cast<const float4 *>(xs + s * xstride + xpad(16 * j));  // no pad inside
-        const float4 p0 = p[0], p1 = p[1], p2 = p[2], p3 = p[3];
-        float t = p0.x;
-        t += p0.y; t += p0.z; t += p0.w;
-        t += p1.x; t += p1.y; t += p1.z; t += p1.w;
-        t += p2.x; t += p2.y; t += p2.z; t += p2.w;
-        t += p3.x; t += p3.y; t += p3.z; t += p3.w;
-        xsum[s * sstride + j] = t;
     }
     __syncthreads();
 }
@@ -316,7 +309,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvArgs a) {
     const int xstride = xpad_len(a.in), sstride = a.in / 16;
     float *xs = sm;                     // [NS][xstride]
     float *xsum = sm + NS * xstride;    // [NS][in/16]
-    __shared__ float red[kThreads / 32];
+    __shared__ float red[kMaxS * (kThreads / 32)];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     stage_x<kV4>(a, xs, xsum, red);
     // ---- rows: a warp per row task ----
@@ -396,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q2k_kernel(const GemvArgs a,
     const int xstride = xpad_len(a.in), sstride = a.in / 16;
     float *xs = sm;
     float *xsum = sm + NS * xstride;
-    __shared__ float red[kThreads / 32];
+    __shared__ float red[kMaxS * (kThreads / 32)];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nb = a.in / QK, ntask = nb * 4;
     const size_t rowBytes = (size_t)nb * Q2K_BYTES;
