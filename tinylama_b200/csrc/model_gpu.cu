@@ -176,11 +176,16 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
 __device__ __forceinline__ void q2_compute1(const Q2Part &p, int n, int h, const float *xs, const float *xsum,
                                             int base, float &acc) {
     const float d = h2f(p.dd & 0xFFFFu), dmin = h2f(p.dd >> 16);
+    // the four scale bytes of this quarter (byte 2it + h of sa, sb), low and high nibbles apart;
+    // a nibble v becomes the float v as the bits 0x4B000000 | v minus 2^23 (exact)
+    const uint32_t S4 = __byte_perm(p.sa, p.sb, h ? 0x7531u : 0x6420u);
+    const uint32_t SL = S4 & 0x0F0F0F0Fu, SH = (S4 >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
-        const uint32_t word = it < 2 ? p.sa : p.sb;
-        const uint32_t sc = (word >> (8 * (2 * (it & 1) + h))) & 0xFFu;
-        const float dl = __fmul_rn(d, (float)(sc & 15u)), ml = __fmul_rn(dmin, (float)(sc >> 4));
+        const uint32_t sel = 0x5440u | (uint32_t)it;  // bytes (nibble it, 0, 0, 0x4B)
+        const float scl = __uint_as_float(__byte_perm(SL, 0x4B00u, sel)) - 8388608.f;
+        const float sch = __uint_as_float(__byte_perm(SH, 0x4B00u, sel)) - 8388608.f;
+        const float dl = __fmul_rn(d, scl), ml = __fmul_rn(dmin, sch);
         const int w0 = base + 128 * n + 32 * it + 16 * h;  // first weight of the sub-block
         float2 F = make_float2(0.f, 0.f);
 #pragma unroll
