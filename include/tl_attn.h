@@ -21,7 +21,8 @@
  *   copy out and return.
  *   Device tier: device pointers, token-major (sequence b, token t, head h, dim d at
  *   ((b*seqLen + t)*H + h)*headDim + d), asynchronous on the caller's cudaStream_t (passed as
- *   void*; NULL = the handle's own stream).
+ *   void*; NULL = the handle's own stream).  The decode calls read q in 16-byte vectors and
+ *   refuse a q that is not 16-byte aligned (TL_ERR_INVALID).
  *   KV cache (owned by the handle, on the device): head-major, K and V each
  *   [nLayer][maxBatch][nHeadKv][maxLen][headDim] of f32 or bf16; one cache slot per
  *   sequence.  The reference's cache is the single-slot, dim-major special case.

@@ -158,6 +158,35 @@ def test_device_error_word_reports_bad_position(env):
         _lib.lib.tl_attn_destroy(h)
 
 
+def test_unaligned_q_is_refused_before_any_launch(env):
+    """The decode kernels read q in 16-byte vectors: a q 4 bytes past a 16-byte boundary is
+    refused on the host with TL_ERR_INVALID (no kernel runs, nothing faults), for the step, the
+    attention-only call and the no-alloc entry point; the handle stays usable."""
+    torch, _lib = env
+    h = create(_lib, 1, 32, 4, 64, 16, 1, 0)
+    try:
+        pos = np.array([3], np.int32)
+        dpos = torch.from_numpy(pos).cuda()
+        f = pos.ctypes.data_as(C.c_void_p)
+        qbuf = torch.zeros(1, 2048 + 4, device="cuda")
+        k = torch.zeros(1, 256, device="cuda")
+        out = torch.empty(1, 2048, device="cuda")
+        bad = C.c_void_p(qbuf.data_ptr() + 4)
+        rc = _lib.lib.tl_decode_step(h, 0, 0, 1, ptr(dpos), f, bad, ptr(k), ptr(k), ptr(out), None)
+        assert rc == _lib.TL_ERR_INVALID and b"16-byte aligned" in _lib.lib.tl_last_error()
+        rc = _lib.lib.tl_decode_attention(h, 0, 0, 1, ptr(dpos), f, bad, ptr(out), None)
+        assert rc == _lib.TL_ERR_INVALID and b"16-byte aligned" in _lib.lib.tl_last_error()
+        kc = torch.zeros(16, 256, device="cuda")
+        rc = _lib.lib.tl_decode_attention_noalloc(bad, ptr(kc), ptr(kc), 0, 32, 4, 64, 16, 1, ptr(dpos), f,
+                                                  ptr(out), None)
+        assert rc == _lib.TL_ERR_INVALID and b"16-byte aligned" in _lib.lib.tl_last_error()
+        q = qbuf[:, :2048].contiguous()
+        _lib.check(_lib.lib.tl_decode_attention(h, 0, 0, 1, ptr(dpos), f, ptr(q), ptr(out), None))
+        _lib.check(_lib.lib.tl_check_device(h, None))
+    finally:
+        _lib.lib.tl_attn_destroy(h)
+
+
 @pytest.mark.parametrize("kvd,S", [(0, 64), (0, 200), (1, 128), (1, 300)])
 def test_prefill_step_batched(env, kvd, S):
     torch, _lib = env

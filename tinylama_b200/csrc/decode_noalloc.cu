@@ -93,6 +93,7 @@ extern "C" int tl_decode_attention_noalloc(const float *q, const void *k_cache, 
                                            void *stream) {
     if (!q || !k_cache || !v_cache || !pos_dev || !pos_host || !out)
         return api_fail(TL_ERR_INVALID, "NULL argument (pos_host is required by the no-alloc entry point)");
+    if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0) return api_fail(TL_ERR_INVALID, "q must be 16-byte aligned");
     if (kvDtype != TL_KV_F32 && kvDtype != TL_KV_BF16) return api_fail(TL_ERR_INVALID, "bad kvDtype");
     if (nHead <= 0 || nHeadKv <= 0 || nHead % nHeadKv != 0)
         return api_fail(TL_ERR_INVALID, "GQA requires head_count divisible by head_count_kv");

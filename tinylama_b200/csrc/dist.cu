@@ -371,6 +371,8 @@ int tl_decode_attention_dist(tl_attn *h, int layer, int slot0, int nseq, const i
                              const int *pos_host, const float *q, float *out, void *stream) {
     if (!h || !pos_dev || !q || !out) return api_fail(TL_ERR_INVALID, "NULL argument");
     if (!h->comm) return api_fail(TL_ERR_INVALID, "tl_dist_init has not been called");
+    // refused before the call takes an epoch, so that every rank refuses the same call alike
+    if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0) return api_fail(TL_ERR_INVALID, "q must be 16-byte aligned");
     if (layer < 0 || layer >= h->nLayer || nseq < 1 || slot0 < 0 || slot0 + nseq > h->maxBatch)
         return api_fail(TL_ERR_INVALID, "layer or slots out of range");
     if (pos_host)

@@ -260,6 +260,9 @@ bool fuse_allowed() {
 int run_decode(tl_attn *h, int layer, int slot0, int nseq, const int *pos_dev, const int *pos_host,
                const float *q, float *out, cudaStream_t s, int pos_offset, float *lse_out,
                const DecodeArgs::Peer *px = nullptr, const RopeAppendArgs *rope = nullptr) {
+    // the decode kernels read a head's q in 16-byte vectors: an unaligned q is refused here
+    // rather than faulting on the device
+    if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0) return fail(TL_ERR_INVALID, "q must be 16-byte aligned");
     Plan p = plan_decode(h, nseq, pos_host, pos_offset, h->maxLen, true, px != nullptr);
     TL_TRY(ensure_partial(h, std::max<size_t>(p.partial_floats, 1)));
     const RopeTab tab = make_rope_tab(h->ropeDim, h->ropeBase);
