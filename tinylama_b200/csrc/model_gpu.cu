@@ -205,6 +205,46 @@ __device__ __forceinline__ void q2_compute1(const Q2Part &p, int n, int h, const
     }
 }
 
+// Two rows' quarters at the same place of x (gate and up, or the two rows of a RoPE pair):
+// the sums of q2_compute1, with each float4 of x and each sub-block sum loaded once for both.
+__device__ __forceinline__ void q2_compute1x2(const Q2Part &pa, const Q2Part &pb, int n, int h, const float *xs,
+                                              const float *xsum, int base, float &acca, float &accb) {
+    const float da = h2f(pa.dd & 0xFFFFu), dmina = h2f(pa.dd >> 16);
+    const float db = h2f(pb.dd & 0xFFFFu), dminb = h2f(pb.dd >> 16);
+    const uint32_t Sa = __byte_perm(pa.sa, pa.sb, h ? 0x7531u : 0x6420u);
+    const uint32_t Sb = __byte_perm(pb.sa, pb.sb, h ? 0x7531u : 0x6420u);
+    const uint32_t SLa = Sa & 0x0F0F0F0Fu, SHa = (Sa >> 4) & 0x0F0F0F0Fu;
+    const uint32_t SLb = Sb & 0x0F0F0F0Fu, SHb = (Sb >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const uint32_t sel = 0x5440u | (uint32_t)it;
+        const float dla = __fmul_rn(da, __uint_as_float(__byte_perm(SLa, 0x4B00u, sel)) - 8388608.f);
+        const float mla = __fmul_rn(dmina, __uint_as_float(__byte_perm(SHa, 0x4B00u, sel)) - 8388608.f);
+        const float dlb = __fmul_rn(db, __uint_as_float(__byte_perm(SLb, 0x4B00u, sel)) - 8388608.f);
+        const float mlb = __fmul_rn(dminb, __uint_as_float(__byte_perm(SHb, 0x4B00u, sel)) - 8388608.f);
+        const int w0 = base + 128 * n + 32 * it + 16 * h;
+        float2 Fa = make_float2(0.f, 0.f), Fb = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float4 xv = *reinterpret_cast<const float4 *>(xs + xpad(w0 + 4 * c));
+            const float2 x01 = make_float2(xv.x, xv.y), x23 = make_float2(xv.z, xv.w);
+            const uint32_t Ta = (((pa.q[c] >> (2 * it)) & 0x03030303u) << 5) | 0x80808080u;
+            const uint32_t Tb = (((pb.q[c] >> (2 * it)) & 0x03030303u) << 5) | 0x80808080u;
+            Fa = ffma2(make_float2(__uint_as_float(__byte_perm(Ta, 0x3F00u, 0x5044u)),
+                                   __uint_as_float(__byte_perm(Ta, 0x3F00u, 0x5144u))), x01, Fa);
+            Fa = ffma2(make_float2(__uint_as_float(__byte_perm(Ta, 0x3F00u, 0x5244u)),
+                                   __uint_as_float(__byte_perm(Ta, 0x3F00u, 0x5344u))), x23, Fa);
+            Fb = ffma2(make_float2(__uint_as_float(__byte_perm(Tb, 0x3F00u, 0x5044u)),
+                                   __uint_as_float(__byte_perm(Tb, 0x3F00u, 0x5144u))), x01, Fb);
+            Fb = ffma2(make_float2(__uint_as_float(__byte_perm(Tb, 0x3F00u, 0x5244u)),
+                                   __uint_as_float(__byte_perm(Tb, 0x3F00u, 0x5344u))), x23, Fb);
+        }
+        const float X = xsum[w0 >> 4];
+        acca = fmaf(dla, 4.f * ((Fa.x + Fa.y) - X), fmaf(-mla, X, acca));
+        accb = fmaf(dlb, 4.f * ((Fb.x + Fb.y) - X), fmaf(-mlb, X, accb));
+    }
+}
+
 template <int NS>
 __device__ __forceinline__ void row_dot(const GMat &M, int row, int in, const float *xs, int xstride,
                                         const float *xsum, int sstride, int S, int lane, float *acc) {
@@ -463,9 +503,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q2k_kernel(const GemvArgs a,
                     const int t = lane + 32 * k;
                     if (t < ntask) {
                         const int n = (t >> 1) & 1, h = t & 1, base = (t >> 2) * QK;
-                        if constexpr (NS == 1) {
+                        if constexpr (NS == 1 && SWI) {
+                            q2_compute1x2(buf[jj][r * TPL + k], buf[jj][RP * TPL + r * TPL + k], n, h, xs, xsum, base,
+                                          acc[r][0], up[r][0]);
+                        } else if constexpr (NS == 1 && RP == 2) {
+                            if (r == 0)  // both rows of the pair at once
+                                q2_compute1x2(buf[jj][k], buf[jj][TPL + k], n, h, xs, xsum, base, acc[0][0], acc[RP - 1][0]);
+                        } else if constexpr (NS == 1) {
                             q2_compute1(buf[jj][r * TPL + k], n, h, xs, xsum, base, acc[r][0]);
-                            if (SWI) q2_compute1(buf[jj][RP * TPL + r * TPL + k], n, h, xs, xsum, base, up[r][0]);
                         } else {
                             q2_compute<NS>(buf[jj][r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, acc[r]);
                             if (SWI) q2_compute<NS>(buf[jj][RP * TPL + r * TPL + k], n, h, xs, xstride, xsum, sstride, base, a.S, up[r]);
