@@ -231,6 +231,11 @@ struct TcShape {
 };
 
 constexpr int TMEM_ALL = 512;
+// Output staging: each softmax warp writes 16 of its rows (64 floats, padded to 68) to shared
+// memory and stores them back as whole 256-byte rows, 2 rows per instruction; a thread storing
+// its own row would touch 32 rows (lines) per instruction.
+constexpr int kStgRow = HD + 4;
+constexpr int kStgFloats = 16 * kStgRow;  // per softmax warp
 constexpr int kIssuers = 3;  // warps that issue tcgen05.mma: one for S, two for P V
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only past 2^8
 
@@ -379,6 +384,7 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
     uint8_t *sK = base + 2 * NQ * TILE_BYTES;            // [NS] tiles
     uint8_t *sV = sK + NS * S_::KV_TILE;                 // [NS] tiles
     B_ *bars = reinterpret_cast<B_ *>(sV + NS * S_::KV_TILE);
+    float *stage = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + (sizeof(B_) + 15) / 16 * 16);
     volatile int *abort_flag = &bars->abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -644,9 +650,35 @@ prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constan
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(&bars->o_free[q]);
-            if (row < p.ntok) {
-                const float inv = l > 0.f ? 1.f / l : 0.f;
-                float *dst = p.out.ptr;
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            float *dst = p.out.ptr;
+            const int wrow0 = row_first + (warp & 3) * 32;  // this warp's first row
+            const int64_t o0 = p.out.at(ti.b, wrow0, ti.h, 0), rs = p.out.st;
+            const bool staged = p.out.sd == 1 && (o0 & 3) == 0 && (rs & 3) == 0 &&
+                                (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+            if (staged) {
+                float *stg = stage + (warp - 4) * kStgFloats;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    if ((lane >> 4) == half) {
+                        float *srow = stg + (lane & 15) * kStgRow;
+#pragma unroll
+                        for (int i = 0; i < HD; i += 4)
+                            *reinterpret_cast<float4 *>(srow + i) =
+                                make_float4(__uint_as_float(orr[i]) * inv, __uint_as_float(orr[i + 1]) * inv,
+                                            __uint_as_float(orr[i + 2]) * inv, __uint_as_float(orr[i + 3]) * inv);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int idx = k * 32 + lane, rr = idx >> 4, c4 = idx & 15;
+                        if (wrow0 + half * 16 + rr < p.ntok)
+                            *reinterpret_cast<float4 *>(dst + o0 + (int64_t)(half * 16 + rr) * rs + 4 * c4) =
+                                *reinterpret_cast<const float4 *>(stg + rr * kStgRow + 4 * c4);
+                    }
+                    __syncwarp();
+                }
+            } else if (row < p.ntok) {
 #pragma unroll
                 for (int i = 0; i < HD; i += 4) {
                     const int64_t o = p.out.at(ti.b, row, ti.h, i);
@@ -719,7 +751,7 @@ cudaError_t launch_shape(const PrefillArgs &a, cudaStream_t s) {
     p.kv_rows_per_slot = a.kv.nHeadKv * a.kv.maxLen;
     p.maxLen = a.kv.maxLen;
     p.err = a.err;
-    const int smem = S_::SMEM + (int)sizeof(Bars<NQ, S_::NS>) + 1024;
+    const int smem = S_::SMEM + (int)sizeof(Bars<NQ, S_::NS>) + 16 + NQ * 4 * kStgFloats * (int)sizeof(float) + 1024;
     auto kern = prefill_tc_kernel<NQ, BN_>;
     static int smem_set[64] = {};
     int dev = 0;
