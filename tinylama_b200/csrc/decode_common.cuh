@@ -216,6 +216,29 @@ __device__ __forceinline__ void peer_store_final(const DecodeArgs &a, int b, int
     }
 }
 
+// Four consecutive columns dd..dd+3 of the final (o, m, l) of (sequence b, head) into slot
+// `rank` of rank r's gather buffer: two 16-byte vector stores of epoch-tagged words (each
+// aligned 8-byte element of a vector store is written single-copy atomically, which is all
+// the reader relies on), and m and l with column 0.
+template <int D>
+__device__ __forceinline__ void peer_store_group(const DecodeArgs &a, int r, int b, int head, int dd, float4 O,
+                                                 float M, float L) {
+    const int64_t row = (int64_t)a.px.rank * a.nseq * a.nHead + (int64_t)b * a.nHead + head;
+    unsigned long long *dst = a.px.gather[r] + row * (D + 2) + dd;
+    const unsigned long long ep = (unsigned long long)a.px.epoch << 32;
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(ep | __float_as_uint(O.x)),
+                 "l"(ep | __float_as_uint(O.y))
+                 : "memory");
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(ep | __float_as_uint(O.z)),
+                 "l"(ep | __float_as_uint(O.w))
+                 : "memory");
+    if (dd == 0) {
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + D), "l"(ep | __float_as_uint(M)),
+                     "l"(ep | __float_as_uint(L))
+                     : "memory");
+    }
+}
+
 // After its own units, every consumer thread of the grid merges a share of this call's
 // (sequence, head, column) elements, reading the ranks' words as they arrive:
 //   M = max_r m_r,  L = sum_r l_r 2^(m_r - M),  ctx = sum_r o_r 2^(m_r - M) / L.

@@ -287,7 +287,12 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
     if (CL > 1) cluster_barrier();
     int j0, j1;
     cluster_share<G, D>(CL, rank, j0, j1);
-    for (int j = j0 + tid; j < j1; j += NW * 32) {
+    // With an exchange across GPUs each thread takes one (group, destination rank) pair, so
+    // that the remote stores of a group go out from R threads at once rather than one after
+    // the other from a single thread (the merge of the group is repeated by those threads).
+    const int R = a.px.nranks > 0 ? a.px.nranks : 1;
+    for (int q = tid; q < (j1 - j0) * R; q += NW * 32) {
+        const int j = j0 + q / R, dest = q - (q / R) * R;
         const int e = 4 * j, h = e / D, dd = e - h * D;
         // the ranks in groups of 8 (registers), merged online: one group for clusters of up to 8
         constexpr int RG = 8;
@@ -332,10 +337,14 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeArgs &a, const Unit
             M = Mn;
         }
         const int head = un.g * G + h;
-        cluster_final<D>(a, un.b, head, dd, O.x, M, L);
-        cluster_final<D>(a, un.b, head, dd + 1, O.y, M, L);
-        cluster_final<D>(a, un.b, head, dd + 2, O.z, M, L);
-        cluster_final<D>(a, un.b, head, dd + 3, O.w, M, L);
+        if (a.px.nranks > 0) {
+            peer_store_group<D>(a, dest, un.b, head, dd, O, M, L);
+        } else {
+            cluster_final<D>(a, un.b, head, dd, O.x, M, L);
+            cluster_final<D>(a, un.b, head, dd + 1, O.y, M, L);
+            cluster_final<D>(a, un.b, head, dd + 2, O.z, M, L);
+            cluster_final<D>(a, un.b, head, dd + 3, O.w, M, L);
+        }
     }
     if (a.fz.k != nullptr) q_stash_write<G, D, NW>(a, un, qst, fz_cs, tid);
     if (CL > 1) cluster_barrier();
