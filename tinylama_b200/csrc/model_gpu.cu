@@ -25,11 +25,14 @@
 // (it = w / 32 % 4), sc byte 8n + 2it + h of the 16 scales.  A lane takes one (block, n, h):
 // 16 bytes of q, i.e. four 16-weight sub-blocks (it = 0..3) that each share one (d*sc, dmin*sc).
 // Per sub-block it forms
-//   F = sum_l (1 + q_l / 4) x_l      (the float 1 + q/4 is the bit pattern 0x3F800000 | q << 21:
-//                                     a shift and a logic op per weight, no int-to-float unit)
+//   F = sum_l (1 + q_l / 4) x_l      (the float 1 + q/4 is the bit pattern 0x3F800000 | q << 21)
 // and adds  d*sc * 4 * (F - X) - dmin*sc * X,  X = sum_l x_l of the sub-block, which the block
-// computes once for all rows in its prologue.  That is three instructions per weight, two of
-// them integer, against 2.6 bits of HBM traffic.
+// computes once for all rows in its prologue.  For one token (the decode step) the bit
+// patterns of four weights come from one word of bytes 0x80 | q << 5 by one byte permutation
+// each, two weights share a packed multiply-add (fma.rn.f32x2), and the two rows of a gate/up
+// or RoPE pair share their loads of x: about two and a half instructions per weight against
+// 2.6 bits of HBM traffic; the several-token prefill path keeps a shift and a logic op per
+// weight and one multiply-add per weight and token.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
